@@ -1,0 +1,158 @@
+// Shared device helpers of the Espalier B200 kernels: status codes, 16-bit float conversions, the 128-point
+// Walsh-Hadamard transform in the reference's butterfly order, bounded mbarrier waits and bulk (TMA) copies.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/espalier_b200.h"
+
+namespace esp {
+
+constexpr float HAD_SCALE = 0.08838834764831845f;   // 1 / sqrt(128), the reference's float literal (dense.cu:23)
+
+enum DType : int { F16 = ESP_DTYPE_F16, BF16 = ESP_DTYPE_BF16, F32 = ESP_DTYPE_F32 };
+
+// Device-side error word of this translation unit: kernels that give up a bounded wait record ESP_ERR_TIMEOUT here
+// and return. Each .cu file exposes its word through ESP_DEFINE_STATUS_READER; esp_device_status() reads them all.
+static __device__ int g_device_status = 0;
+
+#define ESP_DEFINE_STATUS_READER(NAME)                                                          \
+    namespace esp {                                                                            \
+    int status_##NAME(int reset) {                                                             \
+        int v = 0;                                                                             \
+        if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return -1; \
+        if (reset) {                                                                           \
+            const int z = 0;                                                                   \
+            if (cudaMemcpyToSymbol(g_device_status, &z, sizeof(int)) != cudaSuccess) return -1;  \
+        }                                                                                      \
+        return v;                                                                              \
+    }                                                                                          \
+    }
+
+__device__ __forceinline__ void report(int code) { atomicCAS(&g_device_status, 0, code); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// 4 consecutive values of a row as fp32, and back (dense.cu:56-89)
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void load4(const void* p, int dtype, size_t i, float (&v)[4]) {
+    if (dtype == F32) {
+        const float4 u = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+        v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+    } else if (dtype == BF16) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p) + i);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+}
+
+__device__ __forceinline__ void store4(void* p, int dtype, size_t i, const float (&v)[4]) {
+    if (dtype == F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if (dtype == BF16) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) = u;
+    } else {
+        __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(p) + i) = u;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Hadamard-128 of one row, 4 values a lane (lane L holds elements 4L..4L+3): H4 in registers, then xor-partner stages
+// 1..16 across lanes, lower lane a + b, upper lane a - b. The reference's order (dense.cu:43-54), so rotated
+// activations are bit-identical to its own.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void fwht128(float (&v)[4], int lane) {
+    const float a = v[0] + v[1], b = v[0] - v[1], c = v[2] + v[3], d = v[2] - v[3];
+    v[0] = a + c; v[1] = b + d; v[2] = a - c; v[3] = b - d;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
+            v[j] = (lane & m) ? o - v[j] : v[j] + o;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// mbarrier + bulk-copy (TMA) primitives, sm_90+ PTX. Waits are bounded: after `limit` polls the wait reports
+// ESP_ERR_TIMEOUT and returns false, so no kernel can spin forever.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls (a try_wait may suspend briefly): about a second, never forever
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    report(ESP_ERR_TIMEOUT);
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel on the stream start its prologue / wait for the previous one.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+}  // namespace esp

@@ -1,0 +1,178 @@
+// Trellis decode core: 16-bit trellis states -> codebook values, as mma.sync fragments.
+//
+// Format (the reference's experts_grouped.cuh:83-154, 330-339): a 16x16 tile of weights is a circular MSB-first
+// bitstream of 256*K bits (K = bits a weight) stored as 8*K uint32 words (int16 pairs, little-endian). The state of
+// value p (0..255) is the 16 bits ending just before stream bit (p + 1) * K. Value p = 8 * lane + j sits at row
+// (input k) 2t + 8((j >> 1) & 1) + (j & 1) and column (output n) g + 8(j >> 2) of the tile, lane = 4g + t.
+//
+// Design (B200): a lane reads the 2-3 words that hold its eight windows straight from shared memory (the tile was
+// brought in by a bulk copy), aligns them once with a funnel shift and cuts the eight states with constant shifts.
+// The eight values are exactly the lane's A fragment of an m16n8k16 MMA whose M dimension is the tile's 16 output
+// columns and whose N dimension is 8 tokens (weights as A: one MMA per tile per 8 tokens, no register shuffles).
+//
+// Codebooks (kernel ids of the reference, experts_grouped.cuh:23-80): 1 mcg, 3 E2M1, 6 int5, 7 int6.
+//   exact form  (cb_exact): the reference's fp16 values bit for bit (dequant, tests).
+//   kernel form (cb_gemv):  the same values divided by a per-codebook step, exact in fp16, for the GEMVs:
+//                           E2M1 as multiples of C = 0.75 (hardware e2m1 conversion), int5 / int6 as the integer grid
+//                           index q; the GEMV epilogue multiplies its fp32 sums by the step (cb_step).
+#pragma once
+
+#include "common.cuh"
+
+namespace esp {
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// mcg pair (experts_grouped.cuh:64-79): x = s * 0xCBAC1FED; x = (x & 0x8FFF8FFF) ^ 0x3B603B60; v = fp16 lo + fp16 hi
+__device__ __forceinline__ uint32_t mcg2(uint32_t s0, uint32_t s1) {
+    uint32_t x0 = s0 * 0xCBAC1FEDu, x1 = s1 * 0xCBAC1FEDu;
+    x0 = (x0 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    x1 = (x1 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    const uint32_t lo = __byte_perm(x0, x1, 0x5410);
+    const uint32_t hi = __byte_perm(x0, x1, 0x7632);
+    return h2u(__hadd2(u2h(lo), u2h(hi)));
+}
+
+// E2M1 in units of C = 0.75. The reference thresholds |v| at C * {.25, .75, 1.25, 1.75, 2.5, 3.5, 5} with strict '>'
+// (ties go down). Here u = v * fl32(fl32(1/C) * (1 - 2^-20)) in fp32 and the hardware's round-to-nearest-even e2m1
+// conversion: the factor sits just below 1/C, so an exact tie lands below its midpoint and every other fp16 v stays on
+// its side (checked for all 65536 states against the reference's rule). Saturates at 6, keeps the sign of zero.
+constexpr float E2M1_C = 0.75f;
+constexpr float E2M1_INV_C = 0x1.55554p+0f;   // fl32(fl32(1 / 0.75) * fl32(1 - 2^-20))
+
+__device__ __forceinline__ uint32_t e2m1_units2(uint32_t v) {
+    const float2 f = __half22float2(u2h(v));
+    const float a = __fmul_rn(f.x, E2M1_INV_C), b = __fmul_rn(f.y, E2M1_INV_C);
+    uint32_t h;
+    // a -> low half, b -> high half: the packing puts the first source in the upper nibble
+    asm("{ .reg .b8 t; cvt.rn.satfinite.e2m1x2.f32 t, %1, %2; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(h) : "f"(b), "f"(a));
+    return h;
+}
+
+// int5 / int6 grid index q = rintf(fl32(v * k)) (experts_grouped.cuh:39-55). rintf through a magic add:
+// fl32(p + M) with M = 1.5 * 2^23 + 0x6420 rounds p to an integer (ties to even, M even) and leaves the fp16 bits of
+// 1056 + q in the low half-word; one fp16 subtraction of 1056 gives q exactly (|q| <= 31).
+constexpr float INT5_K = 0x1.e62c10p+1f;
+constexpr float INT6_K = 0x1.f660bap+2f;
+constexpr float INT_MAGIC = 12608544.0f;   // 1.5 * 2^23 + 0x6420
+
+template <int CB>
+__device__ __forceinline__ uint32_t int_index2(uint32_t v) {
+    constexpr float k = CB == 6 ? INT5_K : INT6_K;
+    const float2 f = __half22float2(u2h(v));
+    const uint32_t a = __float_as_uint(__fadd_rn(__fmul_rn(f.x, k), INT_MAGIC));
+    const uint32_t b = __float_as_uint(__fadd_rn(__fmul_rn(f.y, k), INT_MAGIC));
+    const __half2 q = u2h(__byte_perm(a, b, 0x5410));
+    return h2u(__hsub2(q, __float2half2_rn(1056.0f)));
+}
+
+// per-codebook factor the kernel form is multiplied by (the reference's c = 3.94921875f / 15 or / 31 in fp32)
+__host__ __device__ __forceinline__ float cb_step(int cb) {
+    return cb == 3 ? E2M1_C : cb == 6 ? 3.94921875f / 15.0f : cb == 7 ? 3.94921875f / 31.0f : 1.0f;
+}
+
+template <int CB>
+__device__ __forceinline__ uint32_t cb_gemv(uint32_t s0, uint32_t s1) {
+    const uint32_t m = mcg2(s0, s1);
+    if constexpr (CB == 1) return m;
+    else if constexpr (CB == 3) return e2m1_units2(m);
+    else return int_index2<CB>(m);
+}
+
+// the reference's fp16 values bit for bit
+template <int CB>
+__device__ __forceinline__ uint32_t cb_exact(uint32_t s0, uint32_t s1) {
+    const uint32_t m = mcg2(s0, s1);
+    if constexpr (CB == 1) {
+        return m;
+    } else if constexpr (CB == 3) {
+        return h2u(__hmul2(u2h(e2m1_units2(m)), __float2half2_rn(E2M1_C)));
+    } else {
+        constexpr float k = CB == 6 ? INT5_K : INT6_K;
+        constexpr float c = 3.94921875f / (CB == 6 ? 15.0f : 31.0f);
+        const float2 v = __half22float2(u2h(m));
+        return h2u(__floats2half2_rn(rintf(__fmul_rn(v.x, k)) * c, rintf(__fmul_rn(v.y, k)) * c));
+    }
+}
+
+// The (codebook, bits) pairs this library instantiates: the reference's set (experts_grouped.cuh:227-229).
+#define ESP_FOR_EACH_CASE(X) \
+    X(1, 1) X(1, 2) X(1, 3) X(1, 4) X(1, 5) X(1, 6) X(1, 7) X(1, 8) \
+    X(3, 1) X(3, 2) X(3, 3) X(6, 2) X(6, 3) X(6, 4) X(7, 3) X(7, 4) X(7, 5)
+
+__host__ __device__ constexpr bool case_supported(int cb, int K) {
+    return (cb == 1 && K >= 1 && K <= 8) || (cb == 3 && K >= 1 && K <= 3) || (cb == 6 && K >= 2 && K <= 4) ||
+           (cb == 7 && K >= 3 && K <= 5);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// A lane's eight states of one tile. `tile` points at the tile's 8K words (shared or global memory).
+// ---------------------------------------------------------------------------------------------------------------
+template <int K>
+__device__ __forceinline__ void tile_states(const uint32_t* tile, int lane, uint32_t (&st)[8]) {
+    constexpr int NB = 256 * K, TW = 8 * K;
+    // the lane's window: stream bits [a, a + 7K + 16), a = 8 lane K + K - 16 (circular)
+    int w0, sh;
+    if constexpr (K == 4) {
+        w0 = (lane + 31) & 31;   // a = 32 lane - 12: word lane - 1, bit 20
+        sh = 20;
+    } else if constexpr (K == 8) {
+        w0 = (2 * lane + 63) & 63;   // a = 64 lane - 8: word 2 lane - 1, bit 24
+        sh = 24;
+    } else {
+        const int a = (8 * lane * K + K - 16 + NB) % NB;
+        w0 = a >> 5;
+        sh = a & 31;
+    }
+    const uint32_t wa = tile[w0];
+    const uint32_t wb = tile[(w0 + 1) % TW];
+    // (hi : lo) = the 64 stream bits from a on, MSB first; state j is bits [jK, jK + 16) of it
+    uint32_t hi, lo, lo2 = 0;
+    if constexpr (K <= 4) {
+        hi = __funnelshift_l(wb, wa, sh);
+        lo = wb << sh;
+    } else {
+        const uint32_t wc = tile[(w0 + 2) % TW];
+        hi = __funnelshift_l(wb, wa, sh);
+        lo = __funnelshift_l(wc, wb, sh);
+        lo2 = wc << sh;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int o = j * K;   // offset of state j from the window's first bit
+        uint32_t s;
+        if (o == 0) s = hi >> 16;
+        else if (o == 8) s = __byte_perm(hi, 0u, 0x4421);
+        else if (o == 16) s = hi & 0xffffu;
+        else if (o < 16) s = (hi >> (16 - o)) & 0xffffu;
+        else if (o == 32) s = lo >> 16;
+        else if (o == 40) s = __byte_perm(lo, 0u, 0x4421);
+        else if (o == 48) s = lo & 0xffffu;
+        else if (o < 48) s = __funnelshift_r(lo, hi, 48 - o) & 0xffffu;
+        else s = __funnelshift_r(lo2, lo, 80 - o) & 0xffffu;
+        st[j] = s;
+    }
+}
+
+// A fragment of m16n8k16 (row-major A = W^T: rows = 16 output columns, cols = 16 inputs) from the eight values:
+// a0 = values 0,1 (col g, k 2t..2t+1); a1 = 4,5 (col g+8); a2 = 2,3 (k 2t+8..); a3 = 6,7.
+template <int CB, int K>
+__device__ __forceinline__ void decode_a(const uint32_t* tile, int lane, uint32_t (&a)[4]) {
+    uint32_t st[8];
+    tile_states<K>(tile, lane, st);
+    a[0] = cb_gemv<CB>(st[0], st[1]);
+    a[1] = cb_gemv<CB>(st[4], st[5]);
+    a[2] = cb_gemv<CB>(st[2], st[3]);
+    a[3] = cb_gemv<CB>(st[6], st[7]);
+}
+
+// D (16 columns x 8 tokens, fp32) += A (16 x 16 fp16) * B (16 x 8 fp16)
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+}  // namespace esp
