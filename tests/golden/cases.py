@@ -81,7 +81,7 @@ DENSE_CASES = [
     ("int5_qkv", 256, [256, 128, 128], 6, 8, (5,), "bf16"),
     ("e2m1_2bit", 256, [128], 3, 4, (3,), "fp16"),
     ("mcg_6bit", 256, [128], 1, 12, (3,), "fp16"),
-    ("int5_3bit", 384, [128, 128], 6, 6, (17,), "bf16"),
+    ("int5_3bit", 512, [128, 128], 6, 6, (17,), "bf16"),
 ]
 
 

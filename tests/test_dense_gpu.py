@@ -97,7 +97,7 @@ def test_config2_block_vs_oracle(dev, M):
 
 
 def test_rows_alone_equal_window(dev):
-    ms, x, _ = _layer("int5_3bit", 384, [128, 128], 6, 6, 17, "bf16", dev)
+    ms, x, _ = _layer("int5_3bit", 512, [128, 128], 6, 6, 17, "bf16", dev)
     d = D.Dense(ms)
     win = d.forward(x).clone()
     for r in range(x.shape[0]):
