@@ -1,0 +1,375 @@
+"""Benchmark of the Espalier B200 decode hot path (one JSON line on rank 0).
+
+Workload ("fused dense decode of one attention/DeltaNet-style block, hidden 2048"): a step is
+one decode step through L = 40 synthetic blocks of q/k/v (2048 -> 4096 + 512 + 512, one fused launch) and o
+(4096 -> 2048), 4-bit trellis with the int5 codebook, random-init seeded weights; block i's o output is block i+1's
+input (q stands in for the attention output). 40 blocks hold 379 MB of compressed weights, 3x the 126 MB L2, so every
+step streams its weights from HBM (no flush needed). The step is captured once in a CUDA graph and replayed.
+
+  value        decode tok/s at batch 1 (whole job: all ranks' tokens / the slowest rank's time)
+  batches      the same at batch 1 / 8 / 32, with compressed-weight GB/s and % of the measured HBM peak
+  roofline     HBM roofline of the fused dense decode kernel on algorithmic (compressed) bytes
+  e2e          the same metric through the public API with host (pinned) input and output copied every step
+  cpu_baseline the reference's decode-then-matmul path restated on the host cores (oracle), bounded sample
+
+N > 1 (torchrun): the dense path runs as data-parallel replicas, one per GPU, no collective on the data path.
+--impl reference: the CPU restatement of the reference path as its own arm (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__  # noqa: E402
+
+HIDDEN, Q, KV, O_IN = 2048, 4096, 512, 4096
+QKV_N = [Q, KV, KV]
+BITS, GRID, KCB = 4, 3, 6            # 4-bit, esp_grid code 3 = int5, kernel codebook 6
+
+
+def block_bytes() -> int:
+    """Algorithmic bytes of one block: trellis + suh + svh of q, k, v and o (9,472,000)."""
+    qkv = HIDDEN * sum(QKV_N) * BITS // 8 + 3 * HIDDEN * 2 + sum(QKV_N) * 2
+    o = O_IN * HIDDEN * BITS // 8 + O_IN * 2 + HIDDEN * 2
+    return qkv + o
+
+
+class Mat:
+    def __init__(self, kin, n, gen, dev):
+        self.trellis = torch.randint(-32768, 32768, (kin // 16, n // 16, 16 * BITS), dtype=torch.int16, device=dev,
+                                     generator=gen)
+        self.suh = (torch.randint(0, 2, (kin,), device=dev, generator=gen) * 2 - 1).half()
+        self.svh = ((torch.randint(0, 2, (n,), device=dev, generator=gen) * 2 - 1).float() *
+                    (0.5 + torch.rand(n, device=dev, generator=gen)) / 64).half()
+        self.K, self.cb, self.in_features, self.out_features = BITS, GRID, kin, n
+
+
+def build_model(layers: int, dev, seed: int = 0):
+    __graft_entry__.load_package()
+    from vllm_espalier_b200 import dense as D
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    blocks = []
+    for _ in range(layers):
+        qkv = D.Dense([Mat(HIDDEN, n, gen, dev) for n in QKV_N])
+        o = D.Dense([Mat(O_IN, HIDDEN, gen, dev)])
+        blocks.append((qkv, o))
+    return blocks
+
+
+class Step:
+    """One decode step at batch R with static buffers (graph-capturable)."""
+
+    def __init__(self, blocks, R, dev):
+        self.blocks, self.R = blocks, R
+        self.x = torch.randn(R, HIDDEN, device=dev).to(torch.bfloat16)
+        self.ys = [(torch.empty(R, sum(QKV_N), dtype=torch.bfloat16, device=dev),
+                    torch.empty(R, HIDDEN, dtype=torch.bfloat16, device=dev)) for _ in blocks]
+        self.graph = None
+
+    @property
+    def out(self):
+        return self.ys[-1][1]
+
+    def eager(self):
+        x = self.x
+        for (qkv, o), (yq, yo) in zip(self.blocks, self.ys):
+            qkv.forward(x, out=yq)
+            o.forward(yq[:, :O_IN], out=yo)
+            x = yo
+
+    def capture(self):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.eager()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.eager()
+
+    def __call__(self):
+        self.graph.replay() if self.graph is not None else self.eager()
+
+    def launches(self) -> int:
+        return 4 * len(self.blocks)      # per block: (rotation + fused decode) for qkv and for o
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(gpu_index)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        self.t0 = self.t1 = None
+
+    def mark(self, start: bool):
+        if start:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        busy = [v for v in sm if v > 0]
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """dram bytes of one fused-dense launch from the committed ncu summary, scaled to the bench's qkv launch."""
+    p = ROOT / "profiles" / "dense_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("bytes_per_block")
+        except (ValueError, KeyError):
+            return None
+    return None
+
+
+def time_steps(step: Step, steps: int, warmup: int, dist, dev) -> float:
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def time_e2e(step: Step, steps: int, warmup: int, dist, dev) -> tuple[float, int, int]:
+    """Host input copied in (pinned, async) and the step's output read back, every step, inside the timed region."""
+    xh = torch.empty_like(step.x, device="cpu").pin_memory()
+    xh.copy_(step.x.cpu())
+    oh = torch.empty_like(step.out, device="cpu").pin_memory()
+
+    def one():
+        step.x.copy_(xh, non_blocking=True)
+        step()
+        oh.copy_(step.out, non_blocking=True)
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, xh.numel() * xh.element_size(), oh.numel() * oh.element_size()
+
+
+def cpu_baseline(blocks, R: int, layers: int, seconds: float = 10.0) -> dict:
+    """The reference's decode-then-matmul path (vllm_espalier/ops.py:45-51: decode W, H(x suh), x @ W, H * svh)
+    restated on the host: trellis decode by the C oracle (OpenMP, all cores), matmul by torch on all cores. Timed on a
+    bounded sample of whole blocks of this workload, scaled to the step."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    host = [[(m.trellis.cpu().numpy(), m.suh.cpu().numpy(), m.svh.cpu().numpy()) for m in d.mats] for blk in blocks
+            for d in blk]
+    h = torch.ones(1, 1)
+    while h.shape[0] < 128:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    H = h / 128 ** 0.5
+
+    def had(v):
+        return (v.view(*v.shape[:-1], -1, 128) @ H).view(v.shape)
+    x = torch.randn(R, HIDDEN).to(torch.bfloat16).float()
+    n_blocks, t0 = 0, time.perf_counter()
+    decode_s = 0.0
+    while True:
+        for qkv_host, o_host in ((host[2 * i], host[2 * i + 1]) for i in range(len(host) // 2)):
+            ys = []
+            for T, su, sv in qkv_host:
+                td = time.perf_counter()
+                W = torch.from_numpy(O.dequant(T, BITS, KCB).astype(np.float32))
+                decode_s += time.perf_counter() - td
+                xh = had(x * torch.from_numpy(su).float()).half().float()
+                ys.append(had(xh @ W) * torch.from_numpy(sv).float())
+            yq = torch.cat(ys, 1).to(torch.bfloat16).float()
+            (T, su, sv), = o_host
+            td = time.perf_counter()
+            W = torch.from_numpy(O.dequant(T, BITS, KCB).astype(np.float32))
+            decode_s += time.perf_counter() - td
+            xh = had(yq[:, :O_IN] * torch.from_numpy(su).float()).half().float()
+            x = (had(xh @ W) * torch.from_numpy(sv).float()).to(torch.bfloat16).float()
+            n_blocks += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        if time.perf_counter() - t0 > seconds:
+            break
+    el = time.perf_counter() - t0
+    per_block = el / n_blocks
+    return {"value": R / (per_block * layers), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n_blocks} of the step's {layers} blocks at batch {R} ({el:.1f} s; decode {decode_s:.1f} s), "
+                      f"scaled to one {layers}-block step",
+            "block_ms": per_block * 1e3}
+
+
+def init_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws <= 1:
+        return None, 0, 1, 0
+    import datetime
+
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist, dist.get_rank(), ws, local
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    dist, rank, ws, local = init_dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    metric = "decode tok/s + compressed-weight HBM GB/s (% of peak) at batch 1/8/32, 1-8 GPU"
+    config = {"workload": f"BASELINE configs[1]: fused dense decode of q/k/v/o blocks, hidden 2048, 4-bit int5, "
+                          f"{a.layers} blocks a step (weights > L2, no flush)", "blocks": a.layers,
+              "parallelism": f"dp{ws} replicas", "graph": not a.no_graph}
+
+    if a.impl == "reference":
+        if rank != 0:
+            if dist:
+                dist.destroy_process_group()
+            return
+        blocks = build_model(a.layers, dev)
+        runs = [cpu_baseline(blocks, 1, a.layers, seconds=max(1.0, a.cpu_seconds / max(a.steps, 1) * 4))
+                for _ in range(max(1, min(a.steps, 3)))]
+        cb = runs[-1]
+        line = {"metric": metric, "value": cb["value"], "unit": "tok/s", "n_gpus": ws, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": 1e3 / cb["value"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random trellis codes)",
+                "config": config, "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    blocks = build_model(a.layers, dev)
+    peak, peak_kind = peaks()
+    clocks = Clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+    nbytes = block_bytes() * a.layers
+    results = {}
+    steps_main = {}
+    for R in (1, 8, 32):
+        st = Step(blocks, R, dev)
+        st.eager()
+        if not a.no_graph:
+            st.capture()
+        steps_main[R] = st
+        clocks.mark(True) if R == 1 else None
+        ms = time_steps(st, a.steps if R == 1 else max(a.steps // 4, 10), a.warmup, dist, dev)
+        clocks.mark(False) if R == 1 else None
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        results[R] = {"tok_s": R * ws / (ms * 1e-3), "ms_per_step": ms, "weight_gbs": gbs,
+                      "hbm_frac": gbs / peak}
+    clk = clocks.stop()
+    e2e_ms, h2d, d2h = time_e2e(steps_main[1], a.steps, a.warmup, dist, dev)
+    pkg = __graft_entry__.load_package()
+    status = pkg._lib.device_status()
+    r1 = results[1]
+    line = {
+        "metric": metric, "value": r1["tok_s"], "unit": "tok/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": r1["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded random trellis codes, N(0,1) bf16 activations)", "config": config,
+        "batches": {str(R): v for R, v in results.items()},
+        "roofline": {"bound": "hbm", "achieved": r1["weight_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": r1["weight_gbs"] / peak, "traffic": traffic_per_launch(),
+                     "note": f"algorithmic compressed bytes {block_bytes()} a block / step time at batch 1; peak "
+                             f"{peak_kind}"},
+        "e2e": {"value": ws * 1 / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": steps_main[1].launches() * a.steps,
+        "clocks": clk, "device_status": status,
+    }
+    if rank == 0 and ws == 1 and not a.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(blocks, 1, a.layers, a.cpu_seconds)
+    for st in steps_main.values():
+        st.graph = None
+    if rank == 0:
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

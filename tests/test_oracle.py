@@ -123,6 +123,17 @@ def test_int_index_magic_exhaustive(cb, six):
     assert np.all(want[differ] == 0) and np.all(np.signbit(want[differ]))
 
 
+def test_int6_single_fma_constant_exhaustive():
+    """int_index2<7> (trellis.cuh) snaps with one FFMA, k' = INT6_K + 1 ulp: the exactly rounded v k' equals
+    rintf(fl32(v k)) for every state (and no such constant exists for int5, which keeps FMUL + FADD)."""
+    mcg = O.codebook_table(1).view(np.float16).astype(np.float64)
+    k = np.float32(float.fromhex("0x1.f660bap+2"))
+    kp = np.array([int(k.view(np.uint32)) + 1], np.uint32).view(np.float32)[0]
+    assert float(kp) == float.fromhex("0x1.f660bcp+2")
+    q = np.rint(mcg * float(kp))            # v * k' is exact in double; one round-half-even
+    assert np.array_equal(q, O.codebook_table(23).view(np.float16).astype(np.float64))
+
+
 def test_int_grid_value_from_index():
     """c * q in fp32 rounded to fp16 (the exact form) for every state."""
     for cb, idx in ((6, 22), (7, 23)):

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -27,6 +28,14 @@ int set_error(int code, const char* fmt, ...) {
 int ok() {
     t_msg[0] = 0;
     return ESP_OK;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("ESPALIER_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 int device_sms() {

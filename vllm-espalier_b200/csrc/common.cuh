@@ -147,6 +147,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Release/acquire fence at GPU scope. One thread executes it after a CTA barrier: the fence is cumulative over the
+// writes the barrier ordered before it, so the whole CTA's stores are published without a fence in every thread.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// 16-byte asynchronous copy global -> shared (L2 only), and the arrive-on of an mbarrier when all of this thread's
+// earlier copies have landed (the arrival counts against the barrier's expected count).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel on the stream start its prologue / wait for the previous one.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

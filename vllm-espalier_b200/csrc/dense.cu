@@ -9,12 +9,14 @@
 //   * rot_kernel writes fp16 H(x * suh_s) / sqrt(128) for every matrix once, in a tile-major layout
 //     [s][k-tile][k-half][row][8] whose per-k-tile slice is one contiguous bulk copy (and bank-conflict free as an MMA
 //     B fragment).
-//   * dense_kernel: one CTA per SM. The layer is a list of units (128-column block, 16-row k-tile) in block-major
-//     order, split into equal contiguous ranges, one per CTA (stream-K), so every SM decodes the same number of
-//     weights. A producer warp streams each unit's 8 tiles (8K words each) and its activation slice into a ring of
-//     shared-memory stages with cp.async.bulk (TMA) and mbarriers; 16 consumer warps (two groups of 8, alternating
-//     k-tiles) decode one tile each per unit straight into the A fragment of mma.sync m16n8k16 (M = 16 output
-//     columns, N = 8 tokens), i.e. the weights are decoded once whatever the number of rows.
+//   * dense_kernel: one CTA per SM (sized so that a second CTA, the next layer's, fits beside it and its programmatic
+//     dependent launch can prefetch that layer's weights while this one finishes). The layer is a list of units
+//     (128-column block, 16-row k-tile) in block-major order, split into equal contiguous ranges, one per CTA
+//     (stream-K), so every SM decodes the same number of weights. A producer warp streams each unit's 8 tiles (8K words
+//     each) and its activation slice into a ring of shared-memory stages with 16-byte cp.async from all 32 lanes,
+//     completing on mbarriers (a bulk copy a unit measured ~40 ns of TMA issue each, too slow for 1 KB units); 8 consumer
+//     warps decode tile w of every unit straight into the A fragment of mma.sync m16n8k16
+//     (M = 16 output columns, N = 8 tokens), i.e. each weight is decoded once whatever the number of rows.
 //   * A block whose k range is split across CTAs is finished by the last CTA to arrive (atomic counter), which adds
 //     the partial sums in CTA order; a block owned by one CTA is finished in place. Finishing = FWHT-128 of the sums,
 //     * step, * H/sqrt(128) * svh, in the reference's order, then the store in y's dtype.
@@ -30,10 +32,19 @@ namespace esp {
 namespace {
 
 constexpr int MAX_SHARDS = 4;
-constexpr int CWARPS = 16;                     // consumer warps (two groups of 8: one warp per tile of a unit)
+#ifndef ESP_DENSE_GROUPS
+#define ESP_DENSE_GROUPS 2
+#endif
+constexpr int GROUPS = ESP_DENSE_GROUPS;       // consumer groups of 8 warps, taking alternate units of a stage
+constexpr int CWARPS = 8 * GROUPS;             // consumer warps: warp w decodes tile w % 8 of its group's units
 constexpr int THREADS = (CWARPS + 1) * 32;     // + one producer warp
-constexpr int UPS = 2;                         // units per pipeline stage
+constexpr int UPS = 8;                         // units per pipeline stage
+constexpr int STAGES = 6;                      // pipeline depth (stages of UPS units)
 constexpr int RED_STRIDE = 132;                // fp32 row stride of the reduction buffer (bank-conflict free)
+#ifndef ESP_DENSE_CTAS_PER_SM
+#define ESP_DENSE_CTAS_PER_SM 1
+#endif
+constexpr int CTAS_PER_SM = ESP_DENSE_CTAS_PER_SM;   // persistent CTAs a streaming multiprocessor
 
 struct DShard {
     const uint32_t* T;   // trellis words [K/16][N/16][8K]
@@ -47,14 +58,18 @@ struct DShard {
 struct DenseParams {
     DShard s[MAX_SHARDS];
     int n;                       // matrices
-    const __half* xh;            // rotated activations [n][KT][2][Mp][8]
+    const __half* xh;            // rotated activations [n][KT][2][Mp][8] (rot_kernel path)
+    const void* x;               // the layer input (fused-rotation path)
+    int x_dtype;
+    long long x_stride;
+    int xh_chunks;               // fused path: 128-input chunks the shared rotation buffer holds
     void* y;
     int y_dtype;
     long long y_stride;
     float* Z;                    // partial sums [2 * G][M][128]
     int* counters;               // [blocks], zero on entry and on exit
     int M, Mp, K, KT, U, G;      // rows, padded rows, inputs, k tiles, units, CTAs
-    int stages;                  // pipeline depth
+    int NB, S;                   // 128-column blocks; CTAs a block (0: whole blocks a CTA)
     float scale;                 // codebook step of the kernel form
 };
 
@@ -96,209 +111,347 @@ __global__ void __launch_bounds__(128) rot_kernel(const __grid_constant__ RotPar
     *reinterpret_cast<uint2*>(p.xh + ((((size_t)s * p.KT + kt) * 2 + h) * p.Mp + m) * 8 + e) = u;
 }
 
+// First unit of CTA c. Split mode (fewer blocks than SMs): block c / S, k-tiles [i KT / S, (i + 1) KT / S) for
+// i = c % S, so no CTA straddles two blocks and each block has exactly S partial sums. Whole mode (S == 0): CTA c owns
+// blocks [c NB / G, (c + 1) NB / G) outright.
 __device__ __forceinline__ long long range_start(int c, const DenseParams& p) {
-    return (long long)c * p.U / p.G;
+    if (p.S == 0) return (long long)c * p.NB / p.G * p.KT;
+    return (long long)(c / p.S) * p.KT + (long long)(c % p.S) * p.KT / p.S;
 }
-__device__ __forceinline__ int cta_of(long long u, const DenseParams& p) {
-    return (int)(((u + 1) * p.G - 1) / p.U);
+
+__device__ __forceinline__ uint2 load_svh(const DShard& S, int bl, int lane) {
+    return *reinterpret_cast<const uint2*>(S.svh + bl * 128 + 4 * lane);
 }
 
 // The finished 4 outputs of lane `lane` of one row of a 128-column block (dense.cu:120-128) and their store.
 __device__ __forceinline__ void finish_store(float (&v)[4], int lane, const DShard& S, int bl, int row,
-                                             const DenseParams& p) {
+                                             const DenseParams& p, uint2 sv) {
     fwht128(v, lane);
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] *= p.scale;
-    const __half* svh = S.svh + bl * 128 + 4 * lane;
-    const uint2 sv = *reinterpret_cast<const uint2*>(svh);
     const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
     const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
     v[0] *= HAD_SCALE * s01.x; v[1] *= HAD_SCALE * s01.y; v[2] *= HAD_SCALE * s23.x; v[3] *= HAD_SCALE * s23.y;
     store4(p.y, p.y_dtype, (size_t)row * p.y_stride + S.col0 + bl * 128 + 4 * lane, v);
 }
 
-template <int CB, int K, int NTG>
+__device__ __forceinline__ int shard_of(int bg, const DenseParams& p) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < MAX_SHARDS; ++i)
+        if (i < p.n && bg >= p.s[i].nb0) s = i;
+    return s;
+}
+
+// Source addresses of unit u (block bg, k-tile kt): its 8 tiles (contiguous) and its activation slice.
+template <int TW, int SLICE_H>
+__device__ __forceinline__ void unit_src(long long u, const DenseParams& p, const uint32_t*& w, const __half*& x) {
+    const int bg = (int)(u / p.KT), kt = (int)(u - (long long)bg * p.KT);
+    const int s = shard_of(bg, p);
+    const DShard& S = p.s[s];
+    w = S.T + ((size_t)kt * S.nb * 8 + (size_t)(bg - S.nb0) * 8) * TW;
+    x = p.xh + ((size_t)s * p.KT + kt) * SLICE_H;
+}
+
+// fp16 H(x[row] * suh) / sqrt(128) of 128-input chunks, stored as MMA B-fragment slices (k-tile, k-half, row, 8): the
+// rot_kernel arithmetic (bit-identical), by one warp into shared memory. Items it = row + MP * chunk_offset; the warp's
+// items are loaded in batches of RB before their transforms so the global-load latency is paid once a batch.
+template <int MP>
+__device__ __forceinline__ void rotate_items(const DenseParams& p, const __half* suh, int chunk0, int nch, int warp,
+                                             int lane, __half* xrot) {
+    constexpr int RB = 4;
+    const int ktl = lane >> 2, h = (lane >> 1) & 1, e = (lane & 1) * 4;     // k = chunk*128 + 16 ktl + 8 h + e
+    const int items = nch * p.M;                                            // real rows only (rows >= M stay zero)
+    for (int base = warp; base < items; base += RB * CWARPS) {
+        float v[RB][4];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            const int it = base + r * CWARPS, row = it % p.M, ch = chunk0 + it / p.M;
+            v[r][0] = v[r][1] = v[r][2] = v[r][3] = 0.f;
+            if (it < items) {
+                const int k = ch * 128 + 4 * lane;
+                load4(p.x, p.x_dtype, (size_t)row * p.x_stride + k, v[r]);
+                const uint2 su = *reinterpret_cast<const uint2*>(suh + k);
+                const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&su.x));
+                const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&su.y));
+                v[r][0] = __fmul_rn(v[r][0], s01.x); v[r][1] = __fmul_rn(v[r][1], s01.y);
+                v[r][2] = __fmul_rn(v[r][2], s23.x); v[r][3] = __fmul_rn(v[r][3], s23.y);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            const int it = base + r * CWARPS, row = it % p.M, cl = it / p.M;
+            if (it >= items) break;
+            fwht128(v[r], lane);
+            const __half2 a = __floats2half2_rn(v[r][0] * HAD_SCALE, v[r][1] * HAD_SCALE);
+            const __half2 b = __floats2half2_rn(v[r][2] * HAD_SCALE, v[r][3] * HAD_SCALE);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(xrot + (size_t)cl * 8 * 2 * MP * 8 + ((ktl * 2 + h) * MP + row) * 8 + e) = u;
+        }
+    }
+}
+
+template <int CB, int K, int NTG, bool FUSED>
 __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant__ DenseParams p) {
     constexpr int TW = 8 * K;                          // words a tile
     constexpr int UNIT_W = 8 * TW;                     // words a unit (8 tiles)
     constexpr int MP = 8 * NTG;
-    constexpr int SLICE_W = MP * 8;                    // words of a unit's activation slice
-    constexpr int STAGE_W = UPS * (UNIT_W + SLICE_W);
+    constexpr int SLICE_W = MP * 8;                    // words of a k-tile's activation slice
+    constexpr int STAGE_W = UPS * (UNIT_W + (FUSED ? 0 : SLICE_W));
     extern __shared__ __align__(128) uint32_t smem[];
-    uint32_t* stage_base = smem;                                        // [stages][STAGE_W]
-    float* red = reinterpret_cast<float*>(smem + (size_t)p.stages * STAGE_W);   // [MP][RED_STRIDE]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + MP * RED_STRIDE);
-    uint64_t* empty = full + p.stages;
-    __shared__ int s_last;
+    float* red = reinterpret_cast<float*>(smem + (size_t)STAGES * STAGE_W);   // [MP][RED_STRIDE]
+    uint32_t* xrot = reinterpret_cast<uint32_t*>(red + MP * RED_STRIDE);      // fused: [chunks][8][2][MP][4]
+    uint64_t* full = reinterpret_cast<uint64_t*>(xrot + (FUSED ? (size_t)p.xh_chunks * 8 * SLICE_W : 0));
+    uint64_t* empty = full + STAGES;
+    __shared__ int s_lastv[2];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
     const long long u0 = range_start(c, p), u1 = range_start(c + 1, p);
-    const int nunits = (int)(u1 - u0);
-    const int nst = (nunits + UPS - 1) / UPS;
+    const int n = (int)(u1 - u0);
+    const int nst = (n + UPS - 1) / UPS;
+    const int bg0 = (int)(u0 / p.KT), kt0 = (int)(u0 - (long long)bg0 * p.KT);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < p.stages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 8 * UPS);
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 32);       // one arrival a producer lane, when its copies of the stage have landed
+            mbar_init(&empty[i], CWARPS);
         }
         fence_mbar_init();
     }
     __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == CWARPS) {   // ---------------- producer ----------------
-        if (lane != 0) return;
-        auto unit_src = [&](long long u, int& bytes) -> const uint32_t* {
-            const int bg = (int)(u / p.KT), kt = (int)(u % p.KT);
-            int s = 0;
-#pragma unroll
-            for (int i = 1; i < MAX_SHARDS; ++i)
-                if (i < p.n && bg >= p.s[i].nb0) s = i;
-            const DShard& S = p.s[s];
-            bytes = UNIT_W * 4;
-            return S.T + ((size_t)kt * (S.nb * 8) + (size_t)(bg - S.nb0) * 8) * TW;
+    if (warp == CWARPS) {   // -------- producer warp: 16-byte async copies, all lanes, arrival on the stage's barrier --------
+        // unit j of a stage: its UNIT_W words in 16-byte pieces spread over the 32 lanes (and its activation slice)
+        int ubg = bg0, ukt = kt0, us = shard_of(bg0, p);
+        auto src_w = [&]() -> const uint32_t* {
+            const DShard& S = p.s[us];
+            return S.T + ((size_t)ukt * S.nb * 8 + (size_t)(ubg - S.nb0) * 8) * TW;
         };
-        auto slice_src = [&](long long u) -> const __half* {
-            const int bg = (int)(u / p.KT), kt = (int)(u % p.KT);
-            int s = 0;
-#pragma unroll
-            for (int i = 1; i < MAX_SHARDS; ++i)
-                if (i < p.n && bg >= p.s[i].nb0) s = i;
-            return p.xh + ((size_t)s * p.KT + kt) * (size_t)(2 * MP * 8);
-        };
-        auto issue = [&](int i, bool weights, bool acts) {
-            const int slot = i % p.stages;
-            uint32_t* st = stage_base + (size_t)slot * STAGE_W;
-            for (int j = 0; j < UPS; ++j) {
-                const long long u = u0 + (long long)i * UPS + j;
-                if (u >= u1) break;
-                int bytes;
-                const uint32_t* src = unit_src(u, bytes);
-                if (weights) bulk_g2s(st + j * UNIT_W, src, UNIT_W * 4, &full[slot]);
-                if (acts) bulk_g2s(st + UPS * UNIT_W + j * SLICE_W, slice_src(u), SLICE_W * 4, &full[slot]);
+        auto src_x = [&]() -> const __half* { return p.xh + ((size_t)us * p.KT + ukt) * (size_t)(2 * MP * 8); };
+        auto step = [&]() {
+            if (++ukt == p.KT) {
+                ukt = 0;
+                ++ubg;
+                if (us + 1 < p.n && ubg >= p.s[us + 1].nb0) ++us;
             }
         };
-        auto stage_bytes = [&](int i) -> uint32_t {
-            const long long a = u0 + (long long)i * UPS;
-            const int n = (int)min((long long)UPS, u1 - a);
-            return (uint32_t)n * (UNIT_W + SLICE_W) * 4u;
+        constexpr int WP = UNIT_W / 4;                 // 16-byte pieces of a unit's tiles
+        constexpr int XP = SLICE_W / 4;                // ... of its activation slice
+        auto fill = [&](int i, int slot, bool w, bool x) {
+            uint32_t* st = smem + (size_t)slot * STAGE_W;
+            const int m = min(UPS, n - i * UPS);
+            for (int j = 0; j < m; ++j, step()) {
+                if (w) {
+                    const uint32_t* src = src_w();
+#pragma unroll
+                    for (int q = lane; q < WP; q += 32) cp_async16(st + j * UNIT_W + q * 4, src + q * 4);
+                }
+                if (x) {
+                    const __half* src = src_x();
+                    for (int q = lane; q < XP; q += 32)
+                        cp_async16(st + UPS * UNIT_W + j * SLICE_W + q * 4, reinterpret_cast<const uint32_t*>(src) + q * 4);
+                }
+            }
+            cp_async_arrive(&full[slot]);
         };
-        const int pre = min(nst, p.stages);
-        for (int i = 0; i < pre; ++i) {   // weights do not depend on the previous kernel: fetch them before waiting
-            mbar_arrive_expect_tx(&full[i], stage_bytes(i));
-            issue(i, true, false);
+        const int pre = min(nst, STAGES);
+        if constexpr (FUSED) {
+            for (int i = 0; i < pre; ++i) fill(i, i, true, false);
+        } else {
+            // weights do not depend on the previous kernel: fetch them first, then (after the wait) the activations
+            const int bgs = ubg, kts = ukt, ss = us;
+            for (int i = 0; i < pre; ++i) {
+                uint32_t* st = smem + (size_t)i * STAGE_W;
+                const int m = min(UPS, n - i * UPS);
+                for (int j = 0; j < m; ++j, step()) {
+                    const uint32_t* src = src_w();
+#pragma unroll
+                    for (int q = lane; q < WP; q += 32) cp_async16(st + j * UNIT_W + q * 4, src + q * 4);
+                }
+            }
+            const int bge = ubg, kte = ukt, se = us;
+            ubg = bgs; ukt = kts; us = ss;
+            pdl_wait();
+            for (int i = 0; i < pre; ++i) fill(i, i, false, true);
+            ubg = bge; ukt = kte; us = se;
         }
-        pdl_wait();
-        for (int i = 0; i < pre; ++i) issue(i, false, true);
-        for (int i = p.stages; i < nst; ++i) {
-            const int slot = i % p.stages;
-            if (!mbar_wait(&empty[slot], ((i / p.stages) - 1) & 1)) return;
-            mbar_arrive_expect_tx(&full[slot], stage_bytes(i));
-            issue(i, true, true);
+        for (int i = STAGES, slot = 0, phase = 0; i < nst; ++i) {
+            if (!mbar_wait(&empty[slot], phase)) return;
+            fill(i, slot, true, !FUSED);
+            if (++slot == STAGES) {
+                slot = 0;
+                phase ^= 1;
+            }
         }
         return;
     }
 
-    // -------------------- consumers: warp w = 8 * grp + wl decodes tile wl of the units of group grp --------------
+    // ---------- consumers: warp w decodes tile w of every unit; even and odd units into separate sums ----------
     pdl_wait();
-    const int grp = warp >> 3, wl = warp & 7;
     const int g = lane >> 2, t = lane & 3;
+    const int grp = warp >> 3, wl = warp & 7;
     constexpr int CT = CWARPS * 32;
 
-    long long u = u0;
-    while (u < u1) {
-        const int bg = (int)(u / p.KT);
-        const long long seg0 = u, seg1 = min(u1, (long long)(bg + 1) * p.KT);
-        float acc[NTG][4];
+    float acc[2][NTG][4];
 #pragma unroll
-        for (int q = 0; q < NTG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
 
-        for (long long uu = seg0 + grp; uu < seg1; uu += 2) {
-            const int li = (int)(uu - u0), stage = li / UPS, slot = stage % p.stages, j = li % UPS;
-            mbar_wait(&full[slot], (stage / p.stages) & 1);
-            const uint32_t* st = stage_base + (size_t)slot * STAGE_W;
-            uint32_t a[4];
-            decode_a<CB, K>(st + j * UNIT_W + wl * TW, lane, a);
-            const uint32_t* xs = st + UPS * UNIT_W + j * SLICE_W;
+    if constexpr (FUSED) {   // rows >= M of the rotated activations are zero once and for all
+        const int words = p.xh_chunks * 8 * SLICE_W;
+        for (int i = threadIdx.x; i < words; i += CT) xrot[i] = 0u;
+        named_sync(1, CT);
+    }
+    int pend_bg[2], npend = 0;     // blocks whose partial sums this CTA wrote, completed after the last segment
+    int bg = bg0, kt = kt0, li = 0, j = 0, slot = 0, phase = 0;
+    bool from_zero = kt0 == 0;     // the current segment starts at the block's first k-tile
+    int chunk0 = 0;                // fused: first 128-input chunk held in xrot
+    bool seg_start = true;
+    while (li < n) {
+        if (FUSED && seg_start) {      // rotate this segment's inputs into shared memory
+            const int seg_kt1 = min(p.KT, kt + (n - li));
+            chunk0 = kt >> 3;
+            const int nch = ((seg_kt1 + 7) >> 3) - chunk0;
+            rotate_items<MP>(p, p.s[shard_of(bg, p)].suh, chunk0, nch, warp, lane, reinterpret_cast<__half*>(xrot));
+            named_sync(1, CT);
+            seg_start = false;
+        }
+        if (j == 0) mbar_wait(&full[slot], phase);
+        const uint32_t* st = smem + (size_t)slot * STAGE_W;
+        const int stage_n = min(UPS, n - (li - j));
+        const int run_end = min(stage_n, j + (p.KT - kt));
+        const int kt_at_j = kt;
+        auto slice = [&](int jj) -> const uint32_t* {
+            if constexpr (FUSED) return xrot + (size_t)(kt_at_j + jj - j - 8 * chunk0) * SLICE_W;
+            else return st + UPS * UNIT_W + jj * SLICE_W;
+        };
+        if (j == 0 && run_end == UPS) {      // the common case: a whole stage inside one segment
 #pragma unroll
-            for (int q = 0; q < NTG; ++q) {
-                const uint32_t b0 = xs[(8 * q + g) * 4 + t];
-                const uint32_t b1 = xs[(MP + 8 * q + g) * 4 + t];
-                mma16816(acc[q], a, b0, b1);
+            for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                const int jj = j2 * GROUPS + grp;
+                uint32_t a[4];
+                decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                const uint32_t* xs = slice(jj);
+#pragma unroll
+                for (int q = 0; q < NTG; ++q)
+                    mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
             }
+        } else {
+            for (int jj = j; jj < run_end; ++jj) {
+                if (GROUPS > 1 && (jj % GROUPS) != grp) continue;
+                uint32_t a[4];
+                decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                const uint32_t* xs = slice(jj);
+#pragma unroll
+                for (int q = 0; q < NTG; ++q) mma16816(acc[0][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+            }
+        }
+        kt += run_end - j;
+        li += run_end - j;
+        j = run_end;
+        if (j == stage_n) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            j = 0;
+            if (++slot == STAGES) {
+                slot = 0;
+                phase ^= 1;
+            }
         }
+        if (kt != p.KT && li != n) continue;
 
-        // ---- segment end: the two groups' sums, group 0 then group 1, into red[token][column] ----
+        // ---- segment end: this warp's 16 columns (even + odd sums) into red[token][column] ----
         const int col = wl * 16 + g;
-        if (grp == 0) {
 #pragma unroll
-            for (int q = 0; q < NTG; ++q) {
-                const int r0 = 8 * q + 2 * t;
-                red[r0 * RED_STRIDE + col] = acc[q][0];
-                red[(r0 + 1) * RED_STRIDE + col] = acc[q][1];
-                red[r0 * RED_STRIDE + col + 8] = acc[q][2];
-                red[(r0 + 1) * RED_STRIDE + col + 8] = acc[q][3];
-            }
-        }
-        named_sync(1, CT);
-        if (grp == 1) {
+        for (int gi = 0; gi < GROUPS; ++gi) {     // group 0's sums, then group 1's added, in that order
+            if (gi == grp) {
 #pragma unroll
-            for (int q = 0; q < NTG; ++q) {
-                const int r0 = 8 * q + 2 * t;
-                red[r0 * RED_STRIDE + col] += acc[q][0];
-                red[(r0 + 1) * RED_STRIDE + col] += acc[q][1];
-                red[r0 * RED_STRIDE + col + 8] += acc[q][2];
-                red[(r0 + 1) * RED_STRIDE + col + 8] += acc[q][3];
+                for (int q = 0; q < NTG; ++q) {
+                    const int r0 = 8 * q + 2 * t;
+                    float* rr = red + r0 * RED_STRIDE + col;
+                    const float v0 = acc[0][q][0] + acc[1][q][0], v1 = acc[0][q][1] + acc[1][q][1];
+                    const float v2 = acc[0][q][2] + acc[1][q][2], v3 = acc[0][q][3] + acc[1][q][3];
+                    if (gi == 0) {
+                        rr[0] = v0; rr[RED_STRIDE] = v1; rr[8] = v2; rr[RED_STRIDE + 8] = v3;
+                    } else {
+                        rr[0] += v0; rr[RED_STRIDE] += v1; rr[8] += v2; rr[RED_STRIDE + 8] += v3;
+                    }
+                }
             }
+            if (GROUPS > 1 && gi + 1 < GROUPS) named_sync(1, CT);
         }
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+            for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
         named_sync(1, CT);
 
-        int s = 0;
-#pragma unroll
-        for (int i = 1; i < MAX_SHARDS; ++i)
-            if (i < p.n && bg >= p.s[i].nb0) s = i;
-        const DShard& S = p.s[s];
-        const int bl = bg - S.nb0;
-        const bool complete = seg0 == (long long)bg * p.KT && seg1 == (long long)(bg + 1) * p.KT;
-        if (complete) {
+        if (from_zero && kt == p.KT) {   // this CTA owns the whole block: finish it now
+            const DShard& S = p.s[shard_of(bg, p)];
+            const int bl = bg - S.nb0;
+            const uint2 sv = load_svh(S, bl, lane);
             for (int r = warp; r < p.M; r += CWARPS) {
                 const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
                 float v[4] = {q.x, q.y, q.z, q.w};
-                finish_store(v, lane, S, bl, r, p);
+                finish_store(v, lane, S, bl, r, p, sv);
             }
-        } else {
-            const long long first_bg = u0 / p.KT;
-            const int slot = 2 * c + (bg == first_bg ? 0 : 1);
-            float* zs = p.Z + (size_t)slot * p.M * 128;
+        } else {                         // partial: store it; the arrival on the block's counter waits for the end
+            float* zs = p.Z + (size_t)c * p.M * 128;     // split mode: one partial a CTA
             for (int r = warp; r < p.M; r += CWARPS)
                 *reinterpret_cast<float4*>(zs + r * 128 + 4 * lane) =
                     *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-            __threadfence();
-            named_sync(1, CT);
-            const int c_lo = cta_of((long long)bg * p.KT, p), c_hi = cta_of((long long)(bg + 1) * p.KT - 1, p);
-            if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[bg], 1) == c_hi - c_lo;
-            named_sync(1, CT);
-            if (s_last) {
-                __threadfence();
-                for (int r = warp; r < p.M; r += CWARPS) {
-                    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int cc = c_lo; cc <= c_hi; ++cc) {
-                        const int sl = 2 * cc + ((long long)bg == range_start(cc, p) / p.KT ? 0 : 1);
-                        const float4 q = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)sl * p.M + r) * 128 +
-                                                                                4 * lane));
-                        sum.x += q.x; sum.y += q.y; sum.z += q.z; sum.w += q.w;
-                    }
-                    float v[4] = {sum.x, sum.y, sum.z, sum.w};
-                    finish_store(v, lane, S, bl, r, p);
-                }
-                if (threadIdx.x == 0) p.counters[bg] = 0;
-            }
+            pend_bg[npend++] = bg;
         }
-        named_sync(1, CT);   // red is reused by the next segment
-        u = seg1;
+        named_sync(1, CT);   // red (and the rotation buffer) are reused by the next segment
+        if (kt == p.KT) {
+            kt = 0;
+            ++bg;
+            from_zero = true;
+        }
+        seg_start = true;
+    }
+
+    if (npend) {
+        named_sync(1, CT);                 // every partial of this CTA is stored
+        if (threadIdx.x < npend) {
+            const int b = pend_bg[threadIdx.x];
+            fence_acq_rel_gpu();           // publish them (cumulative over the barrier) before arriving
+            s_lastv[threadIdx.x] = atomicAdd(&p.counters[b], 1) == p.S - 1;
+            fence_acq_rel_gpu();           // and see the other arrivals' partials if last
+        }
+        named_sync(1, CT);
+        for (int pi = 0; pi < npend; ++pi) {
+            if (!s_lastv[pi]) continue;
+            const int b = pend_bg[pi];
+            const DShard& S = p.s[shard_of(b, p)];
+            const int bl = b - S.nb0;
+            const uint2 sv = load_svh(S, bl, lane);
+            const int c_lo = b * p.S, c_hi = c_lo + p.S - 1;   // the block's CTAs, added in k order
+            for (int r = warp; r < p.M; r += CWARPS) {
+                float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int c8 = c_lo; c8 <= c_hi; c8 += 8) {
+                    float4 q[8];
+#pragma unroll
+                    for (int d = 0; d < 8; ++d)
+                        q[d] = c8 + d <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)(c8 + d) * p.M + r) * 128 +
+                                                                                      4 * lane))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int d = 0; d < 8; ++d)
+                        if (c8 + d <= c_hi) {
+                            sum.x += q[d].x; sum.y += q[d].y; sum.z += q[d].z; sum.w += q[d].w;
+                        }
+                }
+                float v[4] = {sum.x, sum.y, sum.z, sum.w};
+                finish_store(v, lane, S, bl, r, p, sv);
+            }
+            if (threadIdx.x == 0) p.counters[b] = 0;
+        }
     }
 }
 
@@ -352,33 +505,37 @@ __global__ void __launch_bounds__(128) had_kernel(const __half* __restrict__ x, 
     store4(y, F16, i, v);
 }
 
-constexpr int STAGES = 8;
-
-size_t dense_smem_bytes(int K, int ntg) {
+size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks) {
     const int tw = 8 * K, unit_w = 8 * tw, slice_w = 8 * ntg * 8;
-    return (size_t)STAGES * UPS * (unit_w + slice_w) * 4 + (size_t)8 * ntg * RED_STRIDE * 4 + 2 * STAGES * 8;
+    return (size_t)STAGES * UPS * (unit_w + (fused ? 0 : slice_w)) * 4 + (size_t)8 * ntg * RED_STRIDE * 4 +
+           (fused ? (size_t)chunks * 8 * slice_w * 4 : 0) + 2 * STAGES * 8;
 }
 
-template <int CB, int K, int NTG>
+constexpr size_t SMEM_LIMIT = 200 * 1024;
+
+template <int CB, int K, int NTG, bool FUSED>
 int launch_dense(const DenseParams& p, void* stream) {
-    auto kern = dense_kernel<CB, K, NTG>;
-    const size_t smem = dense_smem_bytes(K, NTG);
-    static bool opted = false;
-    if (!opted) {
-        if (int rc = allow_smem(kern, smem)) return rc;
-        opted = true;
+    auto kern = dense_kernel<CB, K, NTG, FUSED>;
+    const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks);
+    static size_t opted = 0;
+    if (smem > opted) {
+        if (int rc = allow_smem(kern, FUSED ? SMEM_LIMIT : smem)) return rc;
+        opted = FUSED ? SMEM_LIMIT : smem;
     }
     return launch(kern, dim3(p.G), dim3(THREADS), smem, stream, true, p);
 }
 
 template <int CB, int K>
-int launch_dense_ntg(const DenseParams& p, void* stream) {
+int launch_dense_ntg(const DenseParams& p, bool fused, void* stream) {
+#define ESP_NTG(N_) \
+    return fused ? launch_dense<CB, K, N_, true>(p, stream) : launch_dense<CB, K, N_, false>(p, stream);
     switch (p.Mp / 8) {
-        case 1: return launch_dense<CB, K, 1>(p, stream);
-        case 2: return launch_dense<CB, K, 2>(p, stream);
-        case 3: return launch_dense<CB, K, 3>(p, stream);
-        default: return launch_dense<CB, K, 4>(p, stream);
+        case 1: ESP_NTG(1)
+        case 2: ESP_NTG(2)
+        case 3: ESP_NTG(3)
+        default: ESP_NTG(4)
     }
+#undef ESP_NTG
 }
 
 }  // namespace
@@ -393,7 +550,7 @@ size_t esp_dense_xh_bytes(int m, int k, int n_mats) {
     return (size_t)n_mats * mp * k * 2;
 }
 
-size_t esp_dense_z_bytes(int m) { return (size_t)2 * device_sms() * m * 128 * 4; }
+size_t esp_dense_z_bytes(int m) { return (size_t)device_sms() * CTAS_PER_SM * m * 128 * 4; }
 
 int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
               int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
@@ -440,28 +597,50 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
     p.K = k;
     p.KT = k / 16;
     p.U = nbt * p.KT;
-    p.G = std::min(device_sms(), p.U);
-    p.stages = STAGES;
+    p.NB = nbt;
+    {
+        const int sms = device_sms() * CTAS_PER_SM;
+        if (nbt >= sms) {            // whole blocks a CTA: no partial sums
+            p.S = 0;
+            p.G = sms;
+        } else {                     // S CTAs a block, each an equal k-slice (at least one k-tile)
+            p.S = std::min(sms / nbt, p.KT);
+            p.G = nbt * p.S;
+        }
+    }
     p.scale = cb_step(cb);
     p.Z = z;
-    const size_t zneed = (size_t)2 * p.G * m * 128 * 4;
-    ESP_REQUIRE(z && z_bytes >= zneed && aligned(z, 16), ESP_ERR_SCRATCH,
+    const size_t zneed = p.S ? (size_t)p.G * m * 128 * 4 : 0;
+    ESP_REQUIRE((zneed == 0 || z) && z_bytes >= zneed && aligned(z, 16), ESP_ERR_SCRATCH,
                 "esp_dense: Z scratch needs %zu bytes, got %zu", zneed, z_bytes);
 
-    r.x = x;
-    r.x_dtype = x_dtype;
-    r.x_stride = x_stride;
-    r.xh = static_cast<__half*>(xh);
-    r.M = m;
-    r.Mp = mp;
-    r.K = k;
-    r.KT = k / 16;
-    if (int rc = launch(rot_kernel, dim3((k / 128 + 3) / 4, mp, n_mats), dim3(128), 0, stream, true, r)) return rc;
+    // the fused path rotates each segment's inputs inside the kernel; a segment spans at most the CTA's units or one
+    // block's k-tiles, plus one chunk of misalignment
+    const long long per_cta = p.S ? (p.KT + p.S - 1) / p.S : (long long)((p.NB + p.G - 1) / p.G) * p.KT;
+    const int max_kt = (int)std::min<long long>(p.KT, per_cta);
+    const int chunks = std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
+    // up to 8 rows the in-kernel rotation is cheaper than a rotation launch; above, its loads serialise per row
+    const bool fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks) <= SMEM_LIMIT;
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.x_stride = x_stride;
+    p.xh_chunks = fused ? chunks : 0;
+    if (!fused) {
+        r.x = x;
+        r.x_dtype = x_dtype;
+        r.x_stride = x_stride;
+        r.xh = static_cast<__half*>(xh);
+        r.M = m;
+        r.Mp = mp;
+        r.K = k;
+        r.KT = k / 16;
+        if (int rc = launch(rot_kernel, dim3((k / 128 + 3) / 4, mp, n_mats), dim3(128), 0, stream, true, r)) return rc;
+    }
 
     int rc = ESP_ERR_UNSUPPORTED;
     switch (cb * 16 + K) {
 #define ESP_DENSE_CASE(CB_, K_) \
-    case CB_ * 16 + K_: rc = launch_dense_ntg<CB_, K_>(p, stream); break;
+    case CB_ * 16 + K_: rc = launch_dense_ntg<CB_, K_>(p, fused, stream); break;
         ESP_FOR_EACH_CASE(ESP_DENSE_CASE)
 #undef ESP_DENSE_CASE
         default: return set_error(ESP_ERR_UNSUPPORTED, "esp_dense: unsupported codebook/width: cb=%d k2=%d", cb, k2);

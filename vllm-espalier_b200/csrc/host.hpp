@@ -13,6 +13,7 @@
 namespace esp {
 
 int set_error(int code, const char* fmt, ...);   // records the message, returns code
+bool pdl_enabled();                               // ESPALIER_PDL (default 1): programmatic dependent launch
 int ok();                                         // clears the message, returns ESP_OK
 int device_sms();                                 // SM count of the current device (cached per device)
 
@@ -40,7 +41,7 @@ int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* s
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    attr[0].val.programmaticStreamSerializationAllowed = (pdl && pdl_enabled()) ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);

@@ -57,12 +57,22 @@ constexpr float INT5_K = 0x1.e62c10p+1f;
 constexpr float INT6_K = 0x1.f660bap+2f;
 constexpr float INT_MAGIC = 12608544.0f;   // 1.5 * 2^23 + 0x6420
 
+// int6 admits a single fused multiply-add: with k' = k + 1 ulp the exactly rounded fl32(v k' + M) equals
+// rintf(fl32(v k)) + M for every one of the 65536 states (an interval of 332 such fp32 k' exists; checked exhaustively).
+// int5 has no such k' (the feasible interval of k is a single point), so it keeps the product's own rounding.
+constexpr float INT6_K_FMA = 0x1.f660bcp+2f;   // INT6_K + 1 ulp
+
 template <int CB>
 __device__ __forceinline__ uint32_t int_index2(uint32_t v) {
-    constexpr float k = CB == 6 ? INT5_K : INT6_K;
     const float2 f = __half22float2(u2h(v));
-    const uint32_t a = __float_as_uint(__fadd_rn(__fmul_rn(f.x, k), INT_MAGIC));
-    const uint32_t b = __float_as_uint(__fadd_rn(__fmul_rn(f.y, k), INT_MAGIC));
+    uint32_t a, b;
+    if constexpr (CB == 7) {
+        a = __float_as_uint(__fmaf_rn(f.x, INT6_K_FMA, INT_MAGIC));
+        b = __float_as_uint(__fmaf_rn(f.y, INT6_K_FMA, INT_MAGIC));
+    } else {
+        a = __float_as_uint(__fadd_rn(__fmul_rn(f.x, INT5_K), INT_MAGIC));
+        b = __float_as_uint(__fadd_rn(__fmul_rn(f.y, INT5_K), INT_MAGIC));
+    }
     const __half2 q = u2h(__byte_perm(a, b, 0x5410));
     return h2u(__hsub2(q, __float2half2_rn(1056.0f)));
 }
