@@ -43,6 +43,7 @@ SIGNATURES = {
     "esp_dequant": (I, [P, I, I, I, I, P, P]),
     "esp_had": (I, [P, I, I, P, P, P, P]),
     "esp_dense": (I, [P, I, L, I, I, C.POINTER(esp_matrix_t), I, I, I, P, I, L, P, S, P, S, P, I, P]),
+    "esp_dense_noalloc": (I, [P, I, L, I, I, C.POINTER(esp_matrix_t), I, I, I, P, I, L, P]),
     "esp_dense_xh_bytes": (S, [I, I, I]),
     "esp_dense_z_bytes": (S, [I]),
 }

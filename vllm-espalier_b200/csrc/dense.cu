@@ -22,6 +22,9 @@
 //     * step, * H/sqrt(128) * svh, in the reference's order, then the store in y's dtype.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 #include "host.hpp"
 #include "trellis.cuh"
@@ -685,3 +688,72 @@ int esp_had(const uint16_t* x, int m, int k, const uint16_t* pre, const uint16_t
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------------
+// Allocation-free dense layer. Some callers cannot allocate device memory at the moment they run a layer: a serving
+// engine that has already handed nearly all of HBM to its KV cache, host code bound only through this C ABI with no
+// allocator of its own, or a path that must not take cudaMalloc's implicit device synchronisation. For them this entry
+// point keeps the dense kernel's scratch (rotated activations, split-K partial sums, arrival counters) in one fixed
+// array of device memory that every GPU loading this library holds until the process exits.
+// ------------------------------------------------------------------------------------------------------------------
+namespace esp {
+namespace {
+constexpr int NOALLOC_MAX_K = 4096;            // input features
+constexpr int NOALLOC_MAX_BLOCKS = 8192;       // 128-column blocks of all matrices of one call (1,048,576 columns)
+constexpr int NOALLOC_MAX_SMS = 160;
+constexpr size_t NOALLOC_Z = (size_t)NOALLOC_MAX_SMS * 32 * 128 * 4;   // partial sums: a CTA x 32 rows x 128 cols
+constexpr size_t NOALLOC_XH = (size_t)MAX_SHARDS * 32 * NOALLOC_MAX_K * 2;
+constexpr size_t NOALLOC_CNT = (size_t)NOALLOC_MAX_BLOCKS * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_Z + NOALLOC_XH + NOALLOC_CNT];   // 3.6 MiB
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {nullptr};
+
+// The array's device address for the current device, looked up once per device (its name in host code is only a
+// host-side stand-in). Returns nullptr after recording the error.
+unsigned char* noalloc_scratch() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        set_error(ESP_ERR_CUDA, "esp_dense_noalloc: no current device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_error(ESP_ERR_CUDA, "esp_dense_noalloc: scratch address: %s", cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_noalloc_addr[dev] = ptr;
+    }
+    return static_cast<unsigned char*>(g_noalloc_addr[dev]);
+}
+}  // namespace
+}  // namespace esp
+
+extern "C" int esp_dense_noalloc(const void* x, int x_dtype, long long x_stride, int m, int k,
+                                 const esp_matrix_t* mats, int n_mats, int k2, int cb, void* y, int y_dtype,
+                                 long long y_stride, void* stream) {
+    using namespace esp;
+    ESP_REQUIRE(mats && n_mats >= 1 && n_mats <= MAX_SHARDS, ESP_ERR_INVALID, "esp_dense_noalloc: 1 to 4 matrices");
+    int nbt = 0;
+    for (int s = 0; s < n_mats; ++s) nbt += mats[s].n / 128;
+    ESP_REQUIRE(k <= NOALLOC_MAX_K, ESP_ERR_INVALID,
+                "esp_dense_noalloc: K=%d exceeds the static scratch limit of %d inputs", k, NOALLOC_MAX_K);
+    ESP_REQUIRE(nbt <= NOALLOC_MAX_BLOCKS, ESP_ERR_INVALID,
+                "esp_dense_noalloc: %d output columns exceed the static scratch limit of %d", nbt * 128,
+                NOALLOC_MAX_BLOCKS * 128);
+    ESP_REQUIRE(device_sms() <= NOALLOC_MAX_SMS, ESP_ERR_INVALID,
+                "esp_dense_noalloc: %d SMs exceed the static scratch limit of %d", device_sms(), NOALLOC_MAX_SMS);
+    unsigned char* base = noalloc_scratch();
+    if (!base) return ESP_ERR_CUDA;
+    float* z = reinterpret_cast<float*>(base);
+    void* xh = base + NOALLOC_Z;
+    int* counters = reinterpret_cast<int*>(base + NOALLOC_Z + NOALLOC_XH);
+    // the counters must start at zero; a call that completes leaves them zero, this also covers one that did not
+    const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)std::max(nbt, 1) * 4, static_cast<cudaStream_t>(stream));
+    ESP_REQUIRE(e == cudaSuccess, ESP_ERR_CUDA, "esp_dense_noalloc: clearing counters: %s", cudaGetErrorString(e));
+    return esp_dense(x, x_dtype, x_stride, m, k, mats, n_mats, k2, cb, y, y_dtype, y_stride, xh, NOALLOC_XH, z,
+                     NOALLOC_Z, counters, NOALLOC_MAX_BLOCKS, stream);
+}
