@@ -45,6 +45,16 @@ SIGNATURES = {
     "esp_dense": (I, [P, I, L, I, I, C.POINTER(esp_matrix_t), I, I, I, P, I, L, P, S, P, S, P, I, P]),
     "esp_dense_noalloc": (I, [P, I, L, I, I, C.POINTER(esp_matrix_t), I, I, I, P, I, L, P]),
     "esp_dense_xh_bytes": (S, [I, I, I]),
+    "esp_route_group": (I, [P, I, L, I, I, P, I, P, I, I, P, P, P, P, P, P, P, I, I, P]),
+    "esp_group": (I, [P, I, I, I, P, P, P, I, I, P]),
+    "esp_group_shared": (I, [P, P, P, I, L, I, P, I, P, P, P, P, P, I, I, I, I, I, P]),
+    "esp_rot_in": (I, [P, I, L, P, P, P, P, P, I, I, I, I, P]),
+    "esp_grouped": (I, [P, P, P, P, P, P, P, P, P, P, I, P, P, P, I, I, P, I, I, I, I, I, I, P]),
+    "esp_moe_gateup": (I, [P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P]),
+    "esp_moe_down": (I, [P, P, P, P, P, P, I, P, P, P, P, I, I, P, P, I, I, I, I, I, P, P, P, P, I, P]),
+    "esp_gateup_epilogue": (I, [P, P, P, P, P, P, I, I, I, I, I, I, F, I, P]),
+    "esp_down_combine": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, P]),
+    "esp_combine": (I, [P, P, P, I, I, I, P]),
     "esp_dense_z_bytes": (S, [I]),
 }
 
@@ -136,6 +146,129 @@ class _Ext:
         _check(y, torch.float16, "y")
         M, K = x.shape
         check(lib().esp_had(x.data_ptr(), M, K, ptr(pre), ptr(post), y.data_ptr(), stream_ptr(x.device)))
+
+
+    # ---- MoE (experts.cpp:44-190, 214-223) ----
+    @staticmethod
+    def route_group(x, gate, sgate, k, shared_id, logits, counter, pick_out, wts_out, uids, ucount, members):
+        _need(x.is_cuda and x.dim() == 2 and x.stride(1) == 1 and gate.is_contiguous(), "x / gate layout")
+        _need(gate.dtype == x.dtype and x.dtype in (torch.bfloat16, torch.float16), "gate and x must share a dtype")
+        _check(logits, torch.float32, "logits")
+        _check(counter, torch.int32, "counter")
+        R, H = x.shape
+        E = gate.shape[0]
+        has = shared_id >= 0
+        _need(logits.numel() >= R * (E + has), "logits scratch too small")
+        maxm = members.size(1) if members.dim() == 2 else R
+        check(lib().esp_route_group(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, H, gate.data_ptr(), E,
+                                    ptr(sgate), int(k), int(shared_id), logits.data_ptr(), counter.data_ptr(),
+                                    pick_out.data_ptr(), wts_out.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
+                                    members.data_ptr(), maxm, uids.numel(), stream_ptr(x.device)))
+
+    @staticmethod
+    def group(pick, uids, ucount, members, R, slots, E):
+        for t, n in ((pick, "pick"), (uids, "uids"), (ucount, "ucount"), (members, "members")):
+            _check(t, torch.int32, n)
+        _need(pick.numel() >= R * slots, "pick too small")
+        _need(uids.numel() >= min(R * slots, E), "uids too small")
+        check(lib().esp_group(pick.data_ptr(), R, slots, E, uids.data_ptr(), ucount.data_ptr(), members.data_ptr(),
+                              members.size(1), uids.numel(), stream_ptr(pick.device)))
+
+    @staticmethod
+    def group_shared(pick_in, wts_in, x, x_stride, gate_w, shared_id, pick_out, wts_out, uids, ucount, members, R,
+                     slots_in, E):
+        _need(x.is_cuda and x.dtype in (torch.bfloat16, torch.float16), "x: bf16/fp16 CUDA")
+        if gate_w is not None:
+            _need(gate_w.dtype == x.dtype and gate_w.is_contiguous() and gate_w.numel() == x.size(1),
+                  "gate_w: x's dtype, [H]")
+        _need(shared_id < 0 or gate_w is not None, "a shared slot needs its gate weight")
+        check(lib().esp_group_shared(pick_in.data_ptr(), wts_in.data_ptr(), x.data_ptr(), DTYPE[x.dtype], int(x_stride),
+                                     x.size(1), ptr(gate_w), int(shared_id), pick_out.data_ptr(), wts_out.data_ptr(),
+                                     uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), R, slots_in, E,
+                                     members.size(1), uids.numel(), stream_ptr(x.device)))
+
+    @staticmethod
+    def rot_in(x, x_stride, pick, suh0, suh1, out0, out1, rows, K, slots, E):
+        _need(x.is_cuda and x.dtype in (torch.bfloat16, torch.float16), "x: bf16/fp16 CUDA")
+        for t, n in ((suh0, "suh0"), (suh1, "suh1"), (out0, "out0"), (out1, "out1")):
+            _check(t, torch.float16, n)
+        check(lib().esp_rot_in(x.data_ptr(), DTYPE[x.dtype], int(x_stride), pick.data_ptr(), suh0.data_ptr(),
+                               suh1.data_ptr(), out0.data_ptr(), out1.data_ptr(), rows, K, slots, E,
+                               stream_ptr(x.device)))
+
+    @staticmethod
+    def grouped(X0, X1, TP0, TP1, B0, B1, C0, C1, uids, ucount, members, Z, mats, K, N, P, SK, slots, nt=4, warps=4,
+                pf=2, lo=2, hi=16, tables=None):
+        """nt / warps / pf / lo / hi are the reference's tile hints (accepted, unused). `tables` = host copies of the
+        k2 / cb tables ([mats][E] each) so unsupported (codebook, width) pairs are refused on the host; if omitted they
+        are read back from the device tables (a synchronisation)."""
+        _check(X0, torch.float16, "X0")
+        _check(Z, torch.float32, "Z")
+        _need(Z.numel() >= mats * SK * P * N, "Z too small")
+        E = TP0.numel()
+        if tables is None:
+            k2h = torch.cat([B0.cpu(), B1.cpu()] if mats == 2 else [B0.cpu()]).to(torch.int32).contiguous()
+            cbh = torch.cat([C0.cpu(), C1.cpu()] if mats == 2 else [C0.cpu()]).to(torch.int32).contiguous()
+        else:
+            k2h, cbh = tables
+        check(lib().esp_grouped(X0.data_ptr(), X1.data_ptr(), TP0.data_ptr(), TP1.data_ptr(), B0.data_ptr(),
+                                B1.data_ptr(), C0.data_ptr(), C1.data_ptr(), k2h.data_ptr(), cbh.data_ptr(), E,
+                                uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), uids.numel(), members.size(1),
+                                Z.data_ptr(), mats, K, N, P, SK, slots, stream_ptr(X0.device)))
+
+    @staticmethod
+    def gateup_epilogue(Z, pick, svh_g, svh_u, suh_d, xd, rows, P, N, SK, slots, E, limit, act_mode):
+        _check(Z, torch.float32, "Z")
+        for t, n in ((svh_g, "svh_g"), (svh_u, "svh_u"), (suh_d, "suh_d"), (xd, "xd")):
+            _check(t, torch.float16, n)
+        lim = float(limit) if limit != float("inf") else float("inf")
+        check(lib().esp_gateup_epilogue(Z.data_ptr(), pick.data_ptr(), svh_g.data_ptr(), svh_u.data_ptr(),
+                                        suh_d.data_ptr(), xd.data_ptr(), rows, P, N, SK, slots, E, lim, int(act_mode),
+                                        stream_ptr(Z.device)))
+
+    @staticmethod
+    def down_epilogue(Z, pick, svh_d, y, rows, P, D, SK, slots, E):
+        check(lib().esp_down_combine(Z.data_ptr(), pick.data_ptr(), svh_d.data_ptr(), y.data_ptr(), None, None, None,
+                                     2, rows, P, D, SK, slots, E, slots, 0, stream_ptr(Z.device)))
+
+    @staticmethod
+    def combine(y, wts, out, rows, D, slots):
+        check(lib().esp_combine(y.data_ptr(), wts.data_ptr(), out.data_ptr(), rows, D, slots, stream_ptr(y.device)))
+
+    @staticmethod
+    def down_combine(Z, pick, svh_d, y, wts, out, rows, P, D, SK, slots, E):
+        _check(out, torch.float32, "out")
+        check(lib().esp_down_combine(Z.data_ptr(), pick.data_ptr(), svh_d.data_ptr(), y.data_ptr(), wts.data_ptr(),
+                                     out.data_ptr(), None, 2, rows, P, D, SK, slots, E, slots, 1, stream_ptr(Z.device)))
+
+    @staticmethod
+    def down_combine2(Z, pick, svh_d, y, wts, out, out_shared, rows, P, D, SK, slots, E, n_routed):
+        _need(out.is_cuda and out.is_contiguous() and out.dtype in DTYPE, "out: contiguous CUDA")
+        if out_shared is not None:
+            _need(out_shared.dtype == out.dtype and out_shared.is_contiguous(), "out_shared: out's dtype")
+        _need(n_routed <= slots, "n_routed <= slots")
+        check(lib().esp_down_combine(Z.data_ptr(), pick.data_ptr(), svh_d.data_ptr(), y.data_ptr(), wts.data_ptr(),
+                                     out.data_ptr(), ptr(out_shared), DTYPE[out.dtype], rows, P, D, SK, slots, E,
+                                     int(n_routed), 1, stream_ptr(Z.device)))
+
+    # ---- the fused B200 pipeline (no reference counterpart: replaces grouped + epilogues) ----
+    @staticmethod
+    def moe_gateup(xg, xu, L, uids, ucount, members, slots, P, S, z, counters, xd):
+        check(lib().esp_moe_gateup(xg.data_ptr(), xu.data_ptr(), L.ptr[0].data_ptr(), L.ptr[1].data_ptr(),
+                                   L.k2[0].data_ptr(), L.k2[1].data_ptr(), L.cb[0].data_ptr(), L.cb[1].data_ptr(),
+                                   L.k2_host_gu.data_ptr(), L.cb_host_gu.data_ptr(), L.E, L.svh_g.data_ptr(),
+                                   L.svh_u.data_ptr(), L.suh_d.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
+                                   members.data_ptr(), uids.numel(), members.size(1), slots, P, L.D, L.I, S,
+                                   z.data_ptr(), counters.data_ptr(), xd.data_ptr(), stream_ptr(xg.device)))
+
+    @staticmethod
+    def moe_down(xd, L, uids, ucount, members, pick, wts, slots, n_routed, rows, y, counters, out, out_shared):
+        check(lib().esp_moe_down(xd.data_ptr(), L.ptr[2].data_ptr(), L.k2[2].data_ptr(), L.cb[2].data_ptr(),
+                                 L.k2_host_d.data_ptr(), L.cb_host_d.data_ptr(), L.E, L.svh_d.data_ptr(),
+                                 uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), uids.numel(), members.size(1),
+                                 pick.data_ptr(), wts.data_ptr(), slots, int(n_routed), rows, L.I, L.D, y.data_ptr(),
+                                 counters.data_ptr(), out.data_ptr(), ptr(out_shared), DTYPE[out.dtype],
+                                 stream_ptr(xd.device)))
 
 
 @lru_cache(1)

@@ -1,0 +1,764 @@
+// Grouped routed + shared expert pipeline for 1..32 tokens of one MoE layer.
+//
+// Reference behaviour (vllm_espalier/experts.py:231-261 routed2 and csrc/experts.cu, experts_grouped.cuh): per slot p =
+// row * slots + j (the row's j-th pick; the shared expert, if any, as the last slot) with expert e = pick[p]:
+//   xg/xu[p]  = fp16(H(x[row] * suh_g/u[e]) / sqrt(128))                       rot_in           experts.cu:97-115
+//   g, u      = xg[p] @ W_gate[e], xu[p] @ W_up[e]  (fp32 sums)                 grouped, mats=2  experts_grouped.cuh
+//   xd[p]     = fp16(H(silu(H(g) h svh_g) * H(u) h svh_u * suh_d) h)            gateup_epilogue  experts.cu:120-162
+//   d         = xd[p] @ W_down[e]                                               grouped, mats=1
+//   y[p]      = H(d) h svh_d (fp32); out[row] = sum_j<n_routed fma(w, y) in slot order; shared = w * y   down_combine2
+// with h = 1/sqrt(128) and H the 128-point Hadamard per 128-block.
+//
+// B200 pipeline (4 launches after this file's kernels: route, rot_in, gate+up, down):
+//   * grouped_kernel decodes, per distinct expert u (uids / members from the routing), the 8 tiles of a 128-column
+//     block b at each k-tile of its k-slice, from a shared-memory stage ring filled by a producer warp with 16-byte
+//     cp.async (the expert's tiles and its members' rotated activation slices), 16 consumer warps, one tile a warp,
+//     mma.sync m16n8k16 with the weights as A (16 output columns) and up to 32 member rows as N. The codebook and width
+//     are dispatched per expert matrix at run time (experts mix E2M1 1/2-bit and int5 3-bit; the shared one is int6).
+//   * MODE_Z writes fp32 partial sums Z[mat][split][p][n] (the reference's `grouped` contract).
+//   * MODE_GATEUP runs gate and up of block b in one CTA, splits K in S equal slices whose partials the last CTA of the
+//     (expert, block) adds in slice order, then applies the SwiGLU epilogue and writes xd.
+//   * MODE_DOWN writes y[p] and, when it is the last of a row's slots to finish a block (a per-(row, block) counter),
+//     combines that row's slots in slot order into out / out_shared.
+// Every sum is in a fixed order that depends on the shapes only, so a token's output never depends on the others.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "host.hpp"
+#include "trellis.cuh"
+
+ESP_DEFINE_STATUS_READER(moe)
+
+namespace esp {
+namespace {
+
+constexpr int GWARPS = 16;                         // consumer warps (two groups of 8)
+constexpr int GTHREADS = (GWARPS + 1) * 32;
+constexpr int GUPS = 8;                            // units a stage
+constexpr int GSTAGES = 4;
+constexpr int GRED = 132;                          // fp32 row stride of the reduction buffers
+
+enum Mode : int { MODE_Z = 0, MODE_GATEUP = 1, MODE_DOWN = 2 };
+
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+
+struct GroupedParams {
+    const int64_t* tp[2];          // trellis pointers a matrix slot [E]
+    const int* k2[2];              // half-bits [E]
+    const int* cb[2];              // kernel codebook ids [E]
+    const __half* X[2];            // rotated inputs [P][K] fp16
+    const int* uids;
+    const int* ucount;
+    const int* members;            // [maxu][maxm] row * 32 + slot, -1 padded
+    int maxm, slots, K, N, P, S, mats, mode, E;
+    float* Z;                      // MODE_Z: [mats][S][P][N]; MODE_GATEUP (S > 1): [2][S][P][N] partials
+    int* counters;                 // MODE_GATEUP: [maxu][N/128]; MODE_DOWN: [rows][N/128]; zero, left zero
+    // MODE_GATEUP epilogue
+    const __half* svh_g;           // [E][N]
+    const __half* svh_u;
+    const __half* suh_d;           // [E][N]
+    __half* xd;                    // [P][N]
+    // MODE_DOWN epilogue and combine
+    const __half* svh_d;           // [E][N]
+    const int* pick;               // [P]
+    const float* wts;              // [P]
+    float* y;                      // [P][N]
+    void* out;                     // [rows][N] out_dtype
+    void* out_shared;              // [rows][N] or null
+    int out_dtype, n_routed;
+};
+
+// ------------------------------------------------------------------------------------------------------------------
+// rot_in (experts.cu:97-115): xg/xu[p] = fp16(H(x[row] * suh[e]) h) for every slot with a valid expert. A warp per
+// (slot, 128-block, matrix).
+// ------------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) rot_in_kernel(const T* __restrict__ x, long long x_stride,
+                                                     const int* __restrict__ pick, const __half* __restrict__ suh0,
+                                                     const __half* __restrict__ suh1, __half* __restrict__ out0,
+                                                     __half* __restrict__ out1, int P, int K, int slots, int E) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int w = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int nblk = K / 128;
+    if (w >= P * nblk * 2) return;
+    const int mat = w / (P * nblk), rem = w % (P * nblk), p = rem / nblk, blk = rem % nblk;
+    const int e = pick[p];
+    if (e < 0 || e >= E) return;
+    const int row = p / slots;
+    const int k = blk * 128 + 4 * lane;
+    const __half* suh = (mat ? suh1 : suh0) + (size_t)e * K + k;
+    const T* xr = x + (size_t)row * x_stride + k;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(to_f<T>(xr[j]), __half2float(suh[j]));
+    fwht128(v, lane);
+    __half* o = (mat ? out1 : out0) + (size_t)p * K + k;
+    const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
+    const __half2 b = __floats2half2_rn(v[2] * HAD_SCALE, v[3] * HAD_SCALE);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(o) = u;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// The grouped decode GEMV
+// ------------------------------------------------------------------------------------------------------------------
+struct CtaWork {
+    int e;            // expert
+    int b;            // 128-column block
+    int split;        // k-slice
+    int mat0, nmats;  // matrix slots this CTA decodes
+    int kt0, nkt;     // k-tiles of the slice
+    int nm;           // members
+};
+
+// decode + MMA of the units [j0, j1) of one stage for one matrix, codebook and width fixed
+template <int CB, int K, int NTG>
+__device__ __forceinline__ void stage_units(const uint32_t* st, const uint32_t* xs0, int j0, int j1, int unit_w,
+                                            int slice_w, int grp, int wl, int lane, int ntg, float (&acc)[2][NTG][4]) {
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int TW = 8 * K;
+    for (int jj = j0 + ((j0 & 1) != grp ? 1 : 0); jj < j1; jj += 2) {
+        uint32_t a[4];
+        decode_a<CB, K>(st + jj * unit_w + wl * TW, lane, a);
+        const uint32_t* xs = xs0 + jj * slice_w;
+#pragma unroll
+        for (int q = 0; q < NTG; ++q)
+            if (q < ntg) mma16816(acc[(jj >> 1) & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(8 * NTG + 8 * q + g) * 4 + t]);
+    }
+}
+
+template <int NTG, int KCAP>
+__device__ __forceinline__ void dispatch_units(int cb, int K, const uint32_t* st, const uint32_t* xs0, int j0, int j1,
+                                               int unit_w, int slice_w, int grp, int wl, int lane, int ntg,
+                                               float (&acc)[2][NTG][4]) {
+    switch (cb * 16 + K) {
+#define ESP_GU_CASE(CB_, K_)                                                                                      \
+    case CB_ * 16 + K_:                                                                                           \
+        if constexpr (K_ <= KCAP) stage_units<CB_, K_, NTG>(st, xs0, j0, j1, unit_w, slice_w, grp, wl, lane, ntg, acc); \
+        else report(ESP_ERR_UNSUPPORTED);                                                                         \
+        break;
+        ESP_FOR_EACH_CASE(ESP_GU_CASE)
+#undef ESP_GU_CASE
+        default: report(ESP_ERR_UNSUPPORTED); break;    // validated on the host; never a trap
+    }
+}
+
+template <int NTG, int KCAP>
+__global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_constant__ GroupedParams p) {
+    constexpr int MP = 8 * NTG;
+    constexpr int UNIT_WMAX = 8 * 8 * KCAP;            // words of a unit at the widest width served
+    constexpr int SLICE_W = MP * 8;                    // words of a k-tile's member slice: [2][MP][8 halves]
+    constexpr int STAGE_W = GUPS * (UNIT_WMAX + SLICE_W);
+    extern __shared__ __align__(128) uint32_t smem[];
+    float* red = reinterpret_cast<float*>(smem + (size_t)GSTAGES * STAGE_W);       // [2][MP][GRED]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * MP * GRED);
+    uint64_t* empty = full + GSTAGES;
+    __shared__ int s_rows[32];        // slot index p of each member
+    __shared__ int s_last;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NB = p.N / 128;
+    const int u = blockIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (u >= p.ucount[0]) return;                    // grid is sized for the most experts a window can touch
+
+    CtaWork w;
+    w.e = p.uids[u];
+    w.b = blockIdx.y;
+    if (p.mode == MODE_Z) {
+        w.split = blockIdx.z % p.S;
+        w.mat0 = blockIdx.z / p.S;
+        w.nmats = 1;
+    } else {
+        w.split = blockIdx.z;
+        w.mat0 = 0;
+        w.nmats = p.mats;
+    }
+    const int KT = p.K / 16;
+    w.kt0 = w.split * KT / p.S;
+    w.nkt = (w.split + 1) * KT / p.S - w.kt0;
+    if (threadIdx.x < 32) {
+        const int code = threadIdx.x < p.maxm ? p.members[u * p.maxm + threadIdx.x] : -1;
+        s_rows[threadIdx.x] = code >= 0 ? (code >> 5) * p.slots + (code & 31) : -1;
+    }
+    int cbs[2], Ks[2];
+    for (int m = 0; m < 2; ++m) {
+        const int mm = min(w.mat0 + m, p.mats - 1);
+        cbs[m] = p.cb[mm][w.e];
+        Ks[m] = p.k2[mm][w.e] / 2;
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < GSTAGES; ++i) {
+            mbar_init(&full[i], 32);
+            mbar_init(&empty[i], GWARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    int nm = 0;
+    while (nm < 32 && s_rows[nm] >= 0) ++nm;           // members come first
+    w.nm = nm;
+    const int ntg = (nm + 7) / 8;
+    const int n = w.nmats * w.nkt;                     // units: matrix-major, then k-tile
+    const int nst = (n + GUPS - 1) / GUPS;
+
+    if (warp == GWARPS) {   // ---------------- producer: 16-byte async copies from all lanes ----------------
+        auto fill = [&](int i, int slot) {
+            uint32_t* st = smem + (size_t)slot * STAGE_W;
+            const int m0 = min(GUPS, n - i * GUPS);
+            for (int j = 0; j < m0; ++j) {
+                const int un = i * GUPS + j, mi = un / w.nkt, kt = w.kt0 + un % w.nkt;
+                const int mat = w.mat0 + mi;
+                const int TW = 8 * Ks[mi];
+                const uint32_t* T = reinterpret_cast<const uint32_t*>(p.tp[mat][w.e]);
+                const uint32_t* src = T + ((size_t)kt * (p.N / 16) + (size_t)w.b * 8) * TW;
+                for (int q = lane; q < 2 * TW; q += 32) cp_async16(st + j * UNIT_WMAX + q * 4, src + q * 4);
+                // member slice of k-tile kt: [h][m][8 halves] from rows X[p_m][16 kt + 8 h ...]
+                const __half* X = p.X[mat];
+                for (int q = lane; q < 2 * nm; q += 32) {
+                    const int m = q >> 1, h = q & 1;
+                    cp_async16(st + GUPS * UNIT_WMAX + j * SLICE_W + (h * MP + m) * 4,
+                               X + (size_t)s_rows[m] * p.K + kt * 16 + h * 8);
+                }
+            }
+            cp_async_arrive(&full[slot]);
+        };
+        const int pre = min(nst, GSTAGES);
+        for (int i = 0; i < pre; ++i) fill(i, i);
+        for (int i = GSTAGES, slot = 0, phase = 0; i < nst; ++i) {
+            if (!mbar_wait(&empty[slot], phase)) return;
+            fill(i, slot);
+            if (++slot == GSTAGES) {
+                slot = 0;
+                phase ^= 1;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int grp = warp >> 3, wl = warp & 7;
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int CT = GWARPS * 32;
+    float acc[2][2][NTG][4];          // [matrix][even/odd unit][token group][4]
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2)
+#pragma unroll
+            for (int q = 0; q < NTG; ++q) acc[m][e2][q][0] = acc[m][e2][q][1] = acc[m][e2][q][2] = acc[m][e2][q][3] = 0.f;
+
+    for (int i = 0, slot = 0, phase = 0; i < nst; ++i) {
+        mbar_wait(&full[slot], phase);
+        const uint32_t* st = smem + (size_t)slot * STAGE_W;
+        const uint32_t* xs0 = st + GUPS * UNIT_WMAX;
+        const int m0 = min(GUPS, n - i * GUPS);
+        // units of this stage by matrix: [u0, u0 + m0) splits at the matrix boundary
+        const int un0 = i * GUPS;
+        const int split_at = min(m0, max(0, w.nkt - un0));     // units of matrix 0 in this stage
+        if (split_at > 0) dispatch_units<NTG, KCAP>(cbs[0], Ks[0], st, xs0, 0, split_at, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[0]);
+        if (m0 > split_at) dispatch_units<NTG, KCAP>(cbs[1], Ks[1], st, xs0, split_at, m0, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[1]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == GSTAGES) {
+            slot = 0;
+            phase ^= 1;
+        }
+    }
+
+    // ---- the CTA's sums: group 0 then group 1, even + odd units, into red[matrix][member][column] ----
+    const int col = wl * 16 + g;
+    for (int gi = 0; gi < 2; ++gi) {
+        if (gi == grp)
+            for (int m = 0; m < w.nmats; ++m)
+#pragma unroll
+                for (int q = 0; q < NTG; ++q) {
+                    const int r0 = 8 * q + 2 * t;
+                    float* rr = red + ((size_t)m * MP + r0) * GRED + col;
+                    const float v0 = acc[m][0][q][0] + acc[m][1][q][0], v1 = acc[m][0][q][1] + acc[m][1][q][1];
+                    const float v2 = acc[m][0][q][2] + acc[m][1][q][2], v3 = acc[m][0][q][3] + acc[m][1][q][3];
+                    if (gi == 0) {
+                        rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
+                    } else {
+                        rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
+                    }
+                }
+        named_sync(1, CT);
+    }
+
+    const int n0 = w.b * 128 + 4 * lane;               // this lane's 4 output columns
+    if (p.mode == MODE_Z) {   // sums of the exact weights: the kernel form times its codebook step
+        const float c0 = cb_step(cbs[0]);
+        for (int m = warp; m < nm; m += GWARPS) {
+            float4 v = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+            v.x *= c0; v.y *= c0; v.z *= c0; v.w *= c0;
+            *reinterpret_cast<float4*>(p.Z + (((size_t)w.mat0 * p.S + w.split) * p.P + s_rows[m]) * p.N + n0) = v;
+        }
+        return;
+    }
+
+    if (p.mode == MODE_GATEUP) {
+        bool finish = true;
+        if (p.S > 1) {   // partials of this slice; the last CTA of (expert, block) adds the slices in order
+            for (int m = warp; m < nm; m += GWARPS)
+                for (int mi = 0; mi < 2; ++mi)
+                    *reinterpret_cast<float4*>(p.Z + (((size_t)mi * p.S + w.split) * p.P + s_rows[m]) * p.N + n0) =
+                        *reinterpret_cast<const float4*>(red + ((size_t)mi * MP + m) * GRED + 4 * lane);
+            named_sync(1, CT);
+            if (threadIdx.x == 0) {
+                fence_acq_rel_gpu();
+                s_last = atomicAdd(&p.counters[u * NB + w.b], 1) == p.S - 1;
+                fence_acq_rel_gpu();
+            }
+            named_sync(1, CT);
+            finish = s_last;
+        }
+        if (!finish) return;
+        const __half* svg = p.svh_g + (size_t)w.e * p.N + n0;
+        const __half* svu = p.svh_u + (size_t)w.e * p.N + n0;
+        const __half* sud = p.suh_d + (size_t)w.e * p.N + n0;
+        for (int m = warp; m < nm; m += GWARPS) {
+            float gv[4], uv[4];
+            if (p.S > 1) {
+                float4 sg = make_float4(0.f, 0.f, 0.f, 0.f), su = sg;
+                for (int s = 0; s < p.S; ++s) {
+                    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)s * p.P + s_rows[m]) * p.N + n0));
+                    const float4 b = __ldcg(reinterpret_cast<const float4*>(p.Z + (((size_t)p.S + s) * p.P + s_rows[m]) * p.N + n0));
+                    sg.x += a.x; sg.y += a.y; sg.z += a.z; sg.w += a.w;
+                    su.x += b.x; su.y += b.y; su.z += b.z; su.w += b.w;
+                }
+                gv[0] = sg.x; gv[1] = sg.y; gv[2] = sg.z; gv[3] = sg.w;
+                uv[0] = su.x; uv[1] = su.y; uv[2] = su.z; uv[3] = su.w;
+            } else {
+                const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                const float4 b = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
+                gv[0] = a.x; gv[1] = a.y; gv[2] = a.z; gv[3] = a.w;
+                uv[0] = b.x; uv[1] = b.y; uv[2] = b.z; uv[3] = b.w;
+            }
+            // the codebook step of each matrix (its kernel form) before the reference's epilogue arithmetic
+            const float cg = cb_step(cbs[0]), cu = cb_step(cbs[1]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                gv[j] *= cg;
+                uv[j] *= cu;
+            }
+            fwht128(gv, lane);
+            fwht128(uv, lane);
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float gg = gv[j] * HAD_SCALE * __half2float(svg[j]);
+                const float uu = uv[j] * HAD_SCALE * __half2float(svu[j]);
+                const float act = gg / (1.f + expf(-gg)) * uu;
+                v[j] = __fmul_rn(act, __half2float(sud[j]));      // never contracted into the butterfly
+            }
+            fwht128(v, lane);
+            __half* o = p.xd + (size_t)s_rows[m] * p.N + n0;
+            const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
+            const __half2 bq = __floats2half2_rn(v[2] * HAD_SCALE, v[3] * HAD_SCALE);
+            uint2 uo;
+            uo.x = *reinterpret_cast<const uint32_t*>(&a);
+            uo.y = *reinterpret_cast<const uint32_t*>(&bq);
+            *reinterpret_cast<uint2*>(o) = uo;
+        }
+        if (p.S > 1 && threadIdx.x == 0) p.counters[u * NB + w.b] = 0;
+        return;
+    }
+
+    // ---- MODE_DOWN: y[p] for this block, then the combine of every row whose slots are all done ----
+    const float cd = cb_step(cbs[0]);
+    const __half* svd = p.svh_d + (size_t)w.e * p.N + n0;
+    for (int m = warp; m < nm; m += GWARPS) {
+        const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+        float v[4] = {a.x * cd, a.y * cd, a.z * cd, a.w * cd};
+        fwht128(v, lane);
+        float4 o;
+        o.x = v[0] * HAD_SCALE * __half2float(svd[0]);
+        o.y = v[1] * HAD_SCALE * __half2float(svd[1]);
+        o.z = v[2] * HAD_SCALE * __half2float(svd[2]);
+        o.w = v[3] * HAD_SCALE * __half2float(svd[3]);
+        *reinterpret_cast<float4*>(p.y + (size_t)s_rows[m] * p.N + n0) = o;
+    }
+    named_sync(1, CT);
+    __shared__ int s_lastrow[32];
+    if (threadIdx.x < nm) {
+        const int pp = s_rows[threadIdx.x], r = pp / p.slots;
+        int valid = 0;
+        for (int j = 0; j < p.slots; ++j) {
+            const int e = p.pick[r * p.slots + j];
+            valid += e >= 0 && e < p.E;
+        }
+        fence_acq_rel_gpu();
+        s_lastrow[threadIdx.x] = atomicAdd(&p.counters[r * NB + w.b], 1) == valid - 1;
+        fence_acq_rel_gpu();
+    }
+    named_sync(1, CT);
+    for (int m = warp; m < nm; m += GWARPS) {
+        if (!s_lastrow[m]) continue;
+        const int r = s_rows[m] / p.slots;
+        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < p.n_routed; ++j) {
+            const int q = r * p.slots + j;
+            const int e = p.pick[q];
+            if (e < 0 || e >= p.E) continue;
+            const float wq = p.wts[q];
+            const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.N + n0));
+            acc4[0] = fmaf(wq, yv.x, acc4[0]);
+            acc4[1] = fmaf(wq, yv.y, acc4[1]);
+            acc4[2] = fmaf(wq, yv.z, acc4[2]);
+            acc4[3] = fmaf(wq, yv.w, acc4[3]);
+        }
+        store4(p.out, p.out_dtype, (size_t)r * p.N + n0, acc4);
+        if (p.out_shared && p.n_routed < p.slots) {
+            const int q = r * p.slots + p.n_routed;
+            const int e = p.pick[q];
+            float sv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (e >= 0 && e < p.E) {
+                const float wq = p.wts[q];
+                const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.N + n0));
+                sv[0] = wq * yv.x; sv[1] = wq * yv.y; sv[2] = wq * yv.z; sv[3] = wq * yv.w;
+            }
+            store4(p.out_shared, p.out_dtype, (size_t)r * p.N + n0, sv);
+        }
+        if (lane == 0) p.counters[r * NB + w.b] = 0;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// The reference's separate epilogue / combine kernels (experts.cu:120-241, 340-393), for drop-in callers of ext().
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void gateup_epilogue_kernel(const float* __restrict__ Z, const int* __restrict__ pick,
+                                       const __half* __restrict__ svh_g, const __half* __restrict__ svh_u,
+                                       const __half* __restrict__ suh_d, __half* __restrict__ xd, int P, int N, int SK,
+                                       int E, float limit, int act_mode) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int p = blockIdx.x, blk = blockIdx.y, lane = threadIdx.x;
+    const int e = pick[p];
+    if (e < 0 || e >= E) return;
+    const int n = blk * 128 + 4 * lane;
+    float gv[4], uv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float sg = 0.f, su = 0.f;
+        for (int s = 0; s < SK; ++s) {
+            sg += Z[((size_t)(0 * SK + s) * P + p) * N + n + j];
+            su += Z[((size_t)(1 * SK + s) * P + p) * N + n + j];
+        }
+        gv[j] = sg;
+        uv[j] = su;
+    }
+    fwht128(gv, lane);
+    fwht128(uv, lane);
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float act;
+        auto bf16r = [](float t) { return __bfloat162float(__float2bfloat16_rn(t)); };
+        if (act_mode == 0) {
+            const float gg = fminf(bf16r(gv[j] * HAD_SCALE * __half2float(svh_g[(size_t)e * N + n + j])), limit);
+            const float uu =
+                fminf(fmaxf(bf16r(uv[j] * HAD_SCALE * __half2float(svh_u[(size_t)e * N + n + j])), -limit), limit);
+            act = bf16r(bf16r(gg / (1.f + expf(-gg))) * uu);
+        } else {
+            const float gg = fminf(gv[j] * HAD_SCALE * __half2float(svh_g[(size_t)e * N + n + j]), limit);
+            const float uu = fminf(fmaxf(uv[j] * HAD_SCALE * __half2float(svh_u[(size_t)e * N + n + j]), -limit), limit);
+            act = gg / (1.f + expf(-gg)) * uu;
+        }
+        v[j] = __fmul_rn(act, __half2float(suh_d[(size_t)e * N + n + j]));
+    }
+    fwht128(v, lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xd[(size_t)p * N + n + j] = __float2half_rn(v[j] * HAD_SCALE);
+}
+
+// down epilogue (+ optional combine into out / out_shared): y[p] = H(sum of splits) h svh_d; out[row] = sum of the
+// first n_routed slots' w * y (fma chain from 0 in slot order), out_shared = w * y of slot n_routed. Block: 32 * slots.
+template <typename TOUT>
+__global__ void down_combine_kernel(const float* __restrict__ Z, const int* __restrict__ pick,
+                                    const __half* __restrict__ svh_d, float* __restrict__ y,
+                                    const float* __restrict__ wts, TOUT* __restrict__ out, TOUT* __restrict__ out_shared,
+                                    int P, int D, int SK, int E, int slots, int n_routed, int combine) {
+    __shared__ float4 part[32][32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x, blk = blockIdx.y;
+    const int k = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blk * 128 + 4 * lane;
+    const int p = r * slots + k;
+    const int e = pick[p];
+    float o[4];
+    if (e >= 0 && e < E) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float s = 0.f;
+            for (int q = 0; q < SK; ++q) s += Z[((size_t)q * P + p) * D + n + j];
+            v[j] = s;
+        }
+        fwht128(v, lane);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            o[j] = v[j] * HAD_SCALE * __half2float(svh_d[(size_t)e * D + n + j]);
+            y[(size_t)p * D + n + j] = o[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = y[(size_t)p * D + n + j];
+    }
+    if (!combine) return;
+    part[k][lane] = make_float4(o[0], o[1], o[2], o[3]);
+    __syncthreads();
+    if (k == 0) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < n_routed; ++q) {
+            const float w = wts[r * slots + q];
+            const float4 u = part[q][lane];
+            acc[0] = fmaf(w, u.x, acc[0]);
+            acc[1] = fmaf(w, u.y, acc[1]);
+            acc[2] = fmaf(w, u.z, acc[2]);
+            acc[3] = fmaf(w, u.w, acc[3]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[(size_t)r * D + n + j] = from_f<TOUT>(acc[j]);
+    } else if (k == n_routed && out_shared != nullptr) {
+        const float w = wts[r * slots + k];
+        const float4 u = part[k][lane];
+        out_shared[(size_t)r * D + n + 0] = from_f<TOUT>(w * u.x);
+        out_shared[(size_t)r * D + n + 1] = from_f<TOUT>(w * u.y);
+        out_shared[(size_t)r * D + n + 2] = from_f<TOUT>(w * u.z);
+        out_shared[(size_t)r * D + n + 3] = from_f<TOUT>(w * u.w);
+    }
+}
+
+// combine (experts.cu:187-195): out[r][d] = sum over slots of fma(w, y) in slot order, fp32.
+__global__ void combine_kernel(const float* __restrict__ y, const float* __restrict__ wts, float* __restrict__ out,
+                               int D, int slots) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x;
+    const int d = blockIdx.y * blockDim.x + threadIdx.x;
+    if (d >= D) return;
+    float acc = 0.f;
+    for (int k = 0; k < slots; ++k) acc = fmaf(wts[r * slots + k], y[((size_t)r * slots + k) * D + d], acc);
+    out[(size_t)r * D + d] = acc;
+}
+
+size_t grouped_smem(int ntg, int kcap) {
+    const int mp = 8 * ntg;
+    return (size_t)GSTAGES * GUPS * (8 * 8 * kcap + mp * 8) * 4 + (size_t)2 * mp * GRED * 4 + 2 * GSTAGES * 8;
+}
+
+template <int NTG, int KCAP>
+int launch_grouped_t(const GroupedParams& p, dim3 grid, void* stream) {
+    auto kern = grouped_kernel<NTG, KCAP>;
+    const size_t smem = grouped_smem(NTG, KCAP);
+    static bool opted = false;
+    if (!opted) {
+        if (int rc = allow_smem(kern, smem)) return rc;
+        opted = true;
+    }
+    return launch(kern, grid, dim3(GTHREADS), smem, stream, true, p);
+}
+
+int launch_grouped(const GroupedParams& p, int ntg, int kmax, int maxu, void* stream) {
+    const dim3 grid((unsigned)maxu, (unsigned)(p.N / 128), (unsigned)(p.mode == MODE_Z ? p.mats * p.S : p.S));
+#define ESP_G(N_)                                                                                   \
+    return kmax <= 4 ? launch_grouped_t<N_, 4>(p, grid, stream) : launch_grouped_t<N_, 8>(p, grid, stream);
+    switch (ntg) {
+        case 1: ESP_G(1)
+        case 2: ESP_G(2)
+        case 3: ESP_G(3)
+        default: ESP_G(4)
+    }
+#undef ESP_G
+}
+
+int check_tables(const int* k2_host, const int* cb_host, int E, int& kmax) {
+    kmax = 0;
+    for (int e = 0; e < E; ++e) {
+        const int k2 = k2_host[e], cb = cb_host[e];
+        ESP_REQUIRE(k2 % 2 == 0 && case_supported(cb, k2 / 2), ESP_ERR_UNSUPPORTED,
+                    "expert %d: no grouped instance for codebook %d at K2 %d", e, cb, k2);
+        kmax = std::max(kmax, k2 / 2);
+    }
+    return ESP_OK;
+}
+
+}  // namespace
+}  // namespace esp
+
+using namespace esp;
+
+extern "C" {
+
+int esp_rot_in(const void* x, int x_dtype, long long x_stride, const int* pick, const uint16_t* suh0,
+               const uint16_t* suh1, uint16_t* out0, uint16_t* out1, int rows, int K, int slots, int E, void* stream) {
+    ESP_REQUIRE(x && pick && suh0 && suh1 && out0 && out1, ESP_ERR_INVALID, "rot_in: null pointer");
+    ESP_REQUIRE(K % 128 == 0 && K > 0, ESP_ERR_INVALID, "K must be a multiple of 128");
+    ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "x: bf16/fp16 CUDA");
+    const int P = rows * slots;
+    if (P == 0) return ok();
+    const dim3 grid((unsigned)((P * (K / 128) * 2 + 3) / 4));
+    int rc;
+    if (x_dtype == ESP_DTYPE_BF16)
+        rc = launch(rot_in_kernel<__nv_bfloat16>, grid, dim3(128), 0, stream, true,
+                    static_cast<const __nv_bfloat16*>(x), x_stride, pick, reinterpret_cast<const __half*>(suh0),
+                    reinterpret_cast<const __half*>(suh1), reinterpret_cast<__half*>(out0),
+                    reinterpret_cast<__half*>(out1), P, K, slots, E);
+    else
+        rc = launch(rot_in_kernel<__half>, grid, dim3(128), 0, stream, true, static_cast<const __half*>(x), x_stride,
+                    pick, reinterpret_cast<const __half*>(suh0), reinterpret_cast<const __half*>(suh1),
+                    reinterpret_cast<__half*>(out0), reinterpret_cast<__half*>(out1), P, K, slots, E);
+    if (rc) return rc;
+    return ok();
+}
+
+// The reference's grouped GEMV: Z[mat][split][p][n] fp32 partial sums (experts.cpp:44-66). k2/cb tables are also
+// passed as host copies (k2_host / cb_host, [mats][E]) so the instance set is checked on the host, not trapped on.
+int esp_grouped(const uint16_t* X0, const uint16_t* X1, const int64_t* TP0, const int64_t* TP1, const int* B0,
+                const int* B1, const int* C0, const int* C1, const int* k2_host, const int* cb_host, int E,
+                const int* uids, const int* ucount, const int* members, int maxu, int maxm, float* Z, int mats, int K,
+                int N, int P, int SK, int slots, void* stream) {
+    ESP_REQUIRE(X0 && TP0 && B0 && C0 && uids && ucount && members && Z && k2_host && cb_host, ESP_ERR_INVALID,
+                "grouped: null pointer");
+    ESP_REQUIRE(mats == 1 || (mats == 2 && X1 && TP1 && B1 && C1), ESP_ERR_INVALID, "grouped: 1 or 2 matrices");
+    ESP_REQUIRE(K % 128 == 0 && N % 128 == 0 && SK >= 1 && (K / 16) >= SK, ESP_ERR_INVALID, "K and N must split evenly");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1, ESP_ERR_INVALID, "grouped: at most 32 members an expert");
+    int kmax = 0, km2 = 0;
+    if (int rc = check_tables(k2_host, cb_host, E, kmax)) return rc;
+    if (mats == 2)
+        if (int rc = check_tables(k2_host + E, cb_host + E, E, km2)) return rc;
+    GroupedParams p = {};
+    p.tp[0] = TP0; p.tp[1] = mats == 2 ? TP1 : TP0;
+    p.k2[0] = B0; p.k2[1] = mats == 2 ? B1 : B0;
+    p.cb[0] = C0; p.cb[1] = mats == 2 ? C1 : C0;
+    p.X[0] = reinterpret_cast<const __half*>(X0);
+    p.X[1] = reinterpret_cast<const __half*>(mats == 2 ? X1 : X0);
+    p.uids = uids; p.ucount = ucount; p.members = members;
+    p.maxm = maxm; p.slots = slots; p.K = K; p.N = N; p.P = P; p.S = SK; p.mats = mats; p.mode = MODE_Z; p.E = E;
+    p.Z = Z;
+    if (int rc = launch_grouped(p, (maxm + 7) / 8, std::max(kmax, km2), maxu, stream)) return rc;
+    return ok();
+}
+
+// Fused gate + up + SwiGLU epilogue: xd[p] for every slot with a valid expert (experts.py routed2 launches 3-4).
+int esp_moe_gateup(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u,
+                   const int* k2_g, const int* k2_u, const int* cb_g, const int* cb_u, const int* k2_host,
+                   const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u, const uint16_t* suh_d,
+                   const int* uids, const int* ucount, const int* members, int maxu, int maxm, int slots, int P, int D,
+                   int I, int S, float* Z, int* counters, uint16_t* xd, void* stream) {
+    ESP_REQUIRE(xg && xu && tp_g && tp_u && svh_g && svh_u && suh_d && uids && ucount && members && xd && k2_host &&
+                    cb_host,
+                ESP_ERR_INVALID, "moe_gateup: null pointer");
+    ESP_REQUIRE(D % 128 == 0 && I % 128 == 0 && S >= 1 && D / 16 >= S, ESP_ERR_INVALID, "moe_gateup: shapes");
+    ESP_REQUIRE(S == 1 || (Z && counters), ESP_ERR_SCRATCH, "moe_gateup: split partials need Z and counters");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1, ESP_ERR_INVALID, "moe_gateup: at most 32 members an expert");
+    int k1 = 0, k2m = 0;
+    if (int rc = check_tables(k2_host, cb_host, E, k1)) return rc;
+    if (int rc = check_tables(k2_host + E, cb_host + E, E, k2m)) return rc;
+    GroupedParams p = {};
+    p.tp[0] = tp_g; p.tp[1] = tp_u; p.k2[0] = k2_g; p.k2[1] = k2_u; p.cb[0] = cb_g; p.cb[1] = cb_u;
+    p.X[0] = reinterpret_cast<const __half*>(xg);
+    p.X[1] = reinterpret_cast<const __half*>(xu);
+    p.uids = uids; p.ucount = ucount; p.members = members;
+    p.maxm = maxm; p.slots = slots; p.K = D; p.N = I; p.P = P; p.S = S; p.mats = 2; p.mode = MODE_GATEUP; p.E = E;
+    p.Z = Z; p.counters = counters;
+    p.svh_g = reinterpret_cast<const __half*>(svh_g);
+    p.svh_u = reinterpret_cast<const __half*>(svh_u);
+    p.suh_d = reinterpret_cast<const __half*>(suh_d);
+    p.xd = reinterpret_cast<__half*>(xd);
+    if (int rc = launch_grouped(p, (maxm + 7) / 8, std::max(k1, k2m), maxu, stream)) return rc;
+    return ok();
+}
+
+// Fused down + combine: out[row] (routed sum, slot order) and out_shared[row] (gated shared slot) in out_dtype.
+int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const int* cb_d, const int* k2_host,
+                 const int* cb_host, int E, const uint16_t* svh_d, const int* uids, const int* ucount,
+                 const int* members, int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed,
+                 int rows, int I, int D, float* y, int* counters, void* out, void* out_shared, int out_dtype,
+                 void* stream) {
+    ESP_REQUIRE(xd && tp_d && svh_d && uids && ucount && members && pick && wts && y && counters && out && k2_host &&
+                    cb_host,
+                ESP_ERR_INVALID, "moe_down: null pointer");
+    ESP_REQUIRE(D % 128 == 0 && I % 128 == 0, ESP_ERR_INVALID, "moe_down: shapes");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && n_routed <= slots, ESP_ERR_INVALID, "moe_down: limits");
+    ESP_REQUIRE(out_dtype >= 0 && out_dtype <= 2, ESP_ERR_INVALID, "moe_down: dtype");
+    int kmax = 0;
+    if (int rc = check_tables(k2_host, cb_host, E, kmax)) return rc;
+    GroupedParams p = {};
+    p.tp[0] = p.tp[1] = tp_d; p.k2[0] = p.k2[1] = k2_d; p.cb[0] = p.cb[1] = cb_d;
+    p.X[0] = p.X[1] = reinterpret_cast<const __half*>(xd);
+    p.uids = uids; p.ucount = ucount; p.members = members;
+    p.maxm = maxm; p.slots = slots; p.K = I; p.N = D; p.P = rows * slots; p.S = 1; p.mats = 1; p.mode = MODE_DOWN;
+    p.E = E; p.counters = counters;
+    p.svh_d = reinterpret_cast<const __half*>(svh_d);
+    p.pick = pick; p.wts = wts; p.y = y; p.out = out; p.out_shared = out_shared; p.out_dtype = out_dtype;
+    p.n_routed = n_routed;
+    if (int rc = launch_grouped(p, (maxm + 7) / 8, kmax, maxu, stream)) return rc;
+    return ok();
+}
+
+int esp_gateup_epilogue(const float* Z, const int* pick, const uint16_t* svh_g, const uint16_t* svh_u,
+                        const uint16_t* suh_d, uint16_t* xd, int rows, int P, int N, int SK, int slots, int E,
+                        float limit, int act_mode, void* stream) {
+    ESP_REQUIRE(Z && pick && svh_g && svh_u && suh_d && xd, ESP_ERR_INVALID, "gateup_epilogue: null pointer");
+    ESP_REQUIRE(N % 128 == 0, ESP_ERR_INVALID, "N must be a multiple of 128");
+    if (rows * slots == 0) return ok();
+    if (int rc = launch(gateup_epilogue_kernel, dim3((unsigned)(rows * slots), (unsigned)(N / 128)), dim3(32), 0,
+                        stream, true, Z, pick, reinterpret_cast<const __half*>(svh_g),
+                        reinterpret_cast<const __half*>(svh_u), reinterpret_cast<const __half*>(suh_d),
+                        reinterpret_cast<__half*>(xd), P, N, SK, E, limit, act_mode))
+        return rc;
+    return ok();
+}
+
+// down_epilogue (combine = 0, out unused), down_combine (fp32 out), down_combine2 (out in out_dtype + out_shared)
+int esp_down_combine(const float* Z, const int* pick, const uint16_t* svh_d, float* y, const float* wts, void* out,
+                     void* out_shared, int out_dtype, int rows, int P, int D, int SK, int slots, int E, int n_routed,
+                     int combine, void* stream) {
+    ESP_REQUIRE(Z && pick && svh_d && y, ESP_ERR_INVALID, "down_combine: null pointer");
+    ESP_REQUIRE(!combine || (wts && out), ESP_ERR_INVALID, "down_combine: weights and out needed");
+    ESP_REQUIRE(slots >= 1 && slots <= 32 && n_routed <= slots, ESP_ERR_INVALID, "at most 32 slots a row");
+    ESP_REQUIRE(D % 128 == 0, ESP_ERR_INVALID, "D must be a multiple of 128");
+    if (rows == 0) return ok();
+    const dim3 grid((unsigned)rows, (unsigned)(D / 128)), block((unsigned)(32 * slots));
+    const __half* sv = reinterpret_cast<const __half*>(svh_d);
+    int rc;
+    if (out_dtype == ESP_DTYPE_BF16)
+        rc = launch(down_combine_kernel<__nv_bfloat16>, grid, block, 0, stream, true, Z, pick, sv, y, wts,
+                    static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(out_shared), P, D, SK, E, slots,
+                    n_routed, combine);
+    else if (out_dtype == ESP_DTYPE_F16)
+        rc = launch(down_combine_kernel<__half>, grid, block, 0, stream, true, Z, pick, sv, y, wts,
+                    static_cast<__half*>(out), static_cast<__half*>(out_shared), P, D, SK, E, slots, n_routed, combine);
+    else
+        rc = launch(down_combine_kernel<float>, grid, block, 0, stream, true, Z, pick, sv, y, wts,
+                    static_cast<float*>(out), static_cast<float*>(out_shared), P, D, SK, E, slots, n_routed, combine);
+    if (rc) return rc;
+    return ok();
+}
+
+int esp_combine(const float* y, const float* wts, float* out, int rows, int D, int slots, void* stream) {
+    ESP_REQUIRE(y && wts && out, ESP_ERR_INVALID, "combine: null pointer");
+    if (rows == 0) return ok();
+    if (int rc = launch(combine_kernel, dim3((unsigned)rows, (unsigned)((D + 255) / 256)), dim3(256), 0, stream, true,
+                        y, wts, out, D, slots))
+        return rc;
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,333 @@
+// MoE routing: router GEMV + softmax / top-k / renormalisation + the shared-expert gate + grouping in one launch, and
+// the grouping kernels the reference exposes separately (group, group_shared).
+//
+// Reference behaviour (vllm_espalier/csrc/route.cu:35-181, experts.cu:23-76, 247-330): logits of the E experts are
+// rounded to bf16 and top-k is taken with the lowest expert id winning ties; the k weights are renormalised to sum 1;
+// the shared slot (id shared_id) gets sigmoid(x . sgate) in fp32; grouping lists the distinct experts in id order and,
+// per expert, its members row * 32 + slot in (row, slot) order, padded with -1.
+//
+// Exactness (BASELINE: expert ids bit-exact against exact routing): each logit is an order-fixed fp64 reduction of the
+// exact bf16 x bf16 products (lane l of a warp sums j = 8 l + 256 i + q, i ascending then q = 0..7, by fused
+// multiply-add from 0; the 32 lane sums meet in an xor tree over offsets 16..1), rounded once to bf16. The CPU oracle
+// (oracle/espalier_oracle.c orc_router_logit) is the same order, so ids match bit for bit, and the fp64 sum is exact
+// to far below bf16 resolution, so they equal the correctly rounded logits' choice. Top-k compares bf16 logit values
+// (exp is monotone), so the choice does not depend on the exponential's last bit.
+//
+// B200 layout: one CTA a logit column (E experts + the shared gate), 8 warps over the rows; the last CTA to arrive
+// (acq_rel counter) does the per-row selection (a warp a row) and the grouping, then resets the counter.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "host.hpp"
+
+ESP_DEFINE_STATUS_READER(route)
+
+namespace esp {
+namespace {
+
+constexpr int RT = 256;                 // threads a CTA
+constexpr int RW = RT / 32;
+constexpr int MAX_K = 16;
+constexpr int MAX_E = 512;              // experts (incl. the shared slot) the grouping handles
+constexpr int MAX_PICKS = 32 * 33;      // rows x slots of one window
+
+template <typename T> __device__ __forceinline__ double to_d(T v);
+template <> __device__ __forceinline__ double to_d<__nv_bfloat16>(__nv_bfloat16 v) { return (double)__bfloat162float(v); }
+template <> __device__ __forceinline__ double to_d<__half>(__half v) { return (double)__half2float(v); }
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+// fp64 logit of one row against one weight row, in the documented order; every lane returns the full sum.
+template <typename T>
+__device__ __forceinline__ double logit64(const T* __restrict__ x, const T* __restrict__ w, int H, int lane) {
+    double acc = 0.0;
+    for (int j0 = 8 * lane; j0 < H; j0 += 256) {
+        const uint4 ux = *reinterpret_cast<const uint4*>(x + j0);
+        const uint4 uw = *reinterpret_cast<const uint4*>(w + j0);
+        const T* a = reinterpret_cast<const T*>(&ux);
+        const T* b = reinterpret_cast<const T*>(&uw);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc = fma(to_d<T>(a[q]), to_d<T>(b[q]), acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+
+__device__ __forceinline__ float round_bf16_d(double v) {
+    // round the fp64 value once to bf16 (nearest even), via the exact fp64 -> bf16 conversion
+    return __bfloat162float(__double2bfloat16(v));
+}
+
+// Distinct experts (< n_ids) of picks[0..n) in id order -> uids / ucount; per expert its members i (row * 32 + slot,
+// i = row * slots + slot) in order, padded with -1 to maxm. One CTA; picks in shared memory.
+__device__ void group_block(const int* sh_pick, int n, int slots, int n_ids, int* __restrict__ uids,
+                            int* __restrict__ ucount, int* __restrict__ members, int maxm, int maxu) {
+    __shared__ int warp_tot[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per = (n_ids + blockDim.x - 1) / blockDim.x;    // ids a thread (<= 2 with 256 threads, 512 ids)
+    int cnt[2] = {0, 0};
+    int used = 0;
+    for (int q = 0; q < per && q < 2; ++q) {
+        const int e = threadIdx.x * per + q;
+        int c = 0;
+        if (e < n_ids)
+            for (int i = 0; i < n; ++i) c += sh_pick[i] == e;
+        cnt[q] = c;
+        used += c > 0;
+    }
+    int inc = used;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = lane < nw ? warp_tot[lane] : 0;
+        int s = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x2 = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += x2;
+        }
+        if (lane < nw) warp_tot[lane] = s - v;
+        if (lane == 31) ucount[0] = s;
+    }
+    __syncthreads();
+    int place = warp_tot[warp] + inc - used;
+    for (int q = 0; q < per && q < 2; ++q) {
+        if (cnt[q] == 0) continue;
+        const int e = threadIdx.x * per + q;
+        if (place < maxu) {
+            uids[place] = e;
+            int j = 0;
+            for (int i = 0; i < n && j < maxm; ++i)
+                if (sh_pick[i] == e) members[place * maxm + j++] = (i / slots) * 32 + (i % slots);
+            for (; j < maxm; ++j) members[place * maxm + j] = -1;
+        }
+        ++place;
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long long x_stride, int R, int H,
+                                                   const T* __restrict__ gate, int E, const T* __restrict__ sgate,
+                                                   int k, int shared_id, float* __restrict__ logits,
+                                                   int* __restrict__ counter, int* __restrict__ pick_out,
+                                                   float* __restrict__ wts_out, int* __restrict__ uids,
+                                                   int* __restrict__ ucount, int* __restrict__ members, int maxm,
+                                                   int maxu) {
+    __shared__ int last;
+    __shared__ int sh_pick[MAX_PICKS];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int has = shared_id >= 0;
+    const int C = E + has;                 // logit columns: experts, then the shared gate
+    const int slots = k + has;
+    const int c = blockIdx.x;
+    const T* w = c < E ? gate + (size_t)c * H : sgate;
+    for (int r = warp; r < R; r += RW) {
+        const double acc = logit64<T>(x + (size_t)r * x_stride, w, H, lane);
+        if (lane == 0) logits[(size_t)r * C + c] = c < E ? round_bf16_d(acc) : (float)acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        fence_acq_rel_gpu();
+        last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+        fence_acq_rel_gpu();
+    }
+    __syncthreads();
+    if (!last) return;
+
+    // per row (a warp a row): top-k of the bf16 logits, lowest id on ties; weights over the selected k
+    for (int r = warp; r < R; r += RW) {
+        const float* lr = logits + (size_t)r * C;
+        float v[MAX_E / 32];
+#pragma unroll
+        for (int q = 0; q < MAX_E / 32; ++q) {
+            const int e = lane + 32 * q;
+            v[q] = e < E ? __ldcg(lr + e) : -INFINITY;
+        }
+        int ids[MAX_K];
+        float lv[MAX_K];
+        for (int t = 0; t < k; ++t) {
+            float bv = -INFINITY;
+            int be = 1 << 30;
+#pragma unroll
+            for (int q = 0; q < MAX_E / 32; ++q) {
+                const int e = lane + 32 * q;
+                if (e < E && (v[q] > bv || (v[q] == bv && e < be))) { bv = v[q]; be = e; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+                if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+            }
+            ids[t] = be;
+            lv[t] = bv;
+#pragma unroll
+            for (int q = 0; q < MAX_E / 32; ++q)
+                if (lane + 32 * q == be) v[q] = -INFINITY;
+        }
+        if (lane == 0) {
+            float p[MAX_K], sum = 0.f;
+            for (int t = 0; t < k; ++t) {
+                p[t] = expf(lv[t] - lv[0]);
+                sum += p[t];
+            }
+            for (int t = 0; t < k; ++t) {
+                pick_out[r * slots + t] = ids[t];
+                wts_out[r * slots + t] = p[t] / sum;
+            }
+            if (has) {
+                pick_out[r * slots + k] = shared_id;
+                wts_out[r * slots + k] = 1.f / (1.f + expf(-__ldcg(lr + E)));
+            }
+        }
+    }
+    __syncthreads();
+    const int n = R * slots;
+    for (int i = threadIdx.x; i < n; i += RT) sh_pick[i] = pick_out[i];
+    __syncthreads();
+    group_block(sh_pick, n, slots, E + has, uids, ucount, members, maxm, maxu);
+    if (threadIdx.x == 0) *counter = 0;
+}
+
+// group (experts.cu:23-76): the grouping of a given pick table.
+__global__ void __launch_bounds__(RT) group_kernel(const int* __restrict__ pick, int n, int slots, int E,
+                                                   int* __restrict__ uids, int* __restrict__ ucount,
+                                                   int* __restrict__ members, int maxm, int maxu) {
+    __shared__ int sh_pick[MAX_PICKS];
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int i = threadIdx.x; i < n; i += RT) sh_pick[i] = pick[i];
+    __syncthreads();
+    group_block(sh_pick, n, slots, E, uids, ucount, members, maxm, maxu);
+}
+
+// group_shared (experts.cu:247-330): routed picks plus the shared slot (weight sigmoid(x . gate_w), fp32 in a fixed
+// per-thread order then a fixed tree), then the grouping.
+template <typename T>
+__global__ void __launch_bounds__(RT) group_shared_kernel(const int* __restrict__ pick_in, const float* __restrict__ wts_in,
+                                                          const T* __restrict__ x, long long x_stride,
+                                                          const T* __restrict__ gate_w, int H, int shared_id,
+                                                          int* __restrict__ pick_out, float* __restrict__ wts_out,
+                                                          int* __restrict__ uids, int* __restrict__ ucount,
+                                                          int* __restrict__ members, int R, int slots_in, int E,
+                                                          int maxm, int maxu) {
+    __shared__ int sh_pick[MAX_PICKS];
+    __shared__ float red[RW];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int has = shared_id >= 0;
+    const int slots = slots_in + has;
+    const int n = R * slots;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < n; i += RT) {
+        const int r = i / slots, q = i % slots;
+        const int e = q < slots_in ? pick_in[r * slots_in + q] : shared_id;
+        sh_pick[i] = e;
+        pick_out[i] = e;
+        if (q < slots_in) wts_out[i] = wts_in[r * slots_in + q];
+    }
+    if (has) {
+        for (int r = 0; r < R; ++r) {
+            float acc = 0.f;
+            for (int j = threadIdx.x; j < H; j += RT) acc = fmaf(to_f<T>(x[(size_t)r * x_stride + j]), to_f<T>(gate_w[j]), acc);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) red[warp] = acc;
+            __syncthreads();
+            if (warp == 0) {
+                float v = lane < RW ? red[lane] : 0.f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) wts_out[r * slots + slots_in] = 1.f / (1.f + expf(-v));
+            }
+            __syncthreads();
+        }
+    }
+    __syncthreads();
+    group_block(sh_pick, n, slots, E, uids, ucount, members, maxm, maxu);
+}
+
+}  // namespace
+}  // namespace esp
+
+using namespace esp;
+
+extern "C" {
+
+int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                    const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                    int* uids, int* ucount, int* members, int maxm, int maxu, void* stream) {
+    ESP_REQUIRE(x && gate && logits && counter && pick_out && wts_out && uids && ucount && members, ESP_ERR_INVALID,
+                "route_group: null pointer");
+    const int has = shared_id >= 0;
+    ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "route_group: x must be bf16 or fp16");
+    ESP_REQUIRE(E >= 1 && E + has <= MAX_E && k >= 1 && k <= MAX_K && k <= E && H % 256 == 0 && H > 0, ESP_ERR_INVALID,
+                "route_group: shape limits");
+    ESP_REQUIRE(R >= 1 && R * (k + has) <= MAX_PICKS && k + has <= 32, ESP_ERR_INVALID, "route_group: window too large");
+    ESP_REQUIRE(!has || sgate, ESP_ERR_INVALID, "the shared gate weight is needed with a shared slot");
+    ESP_REQUIRE(aligned(x, 16) && aligned(gate, 16) && (!has || aligned(sgate, 16)) && x_stride % 8 == 0,
+                ESP_ERR_INVALID, "route_group: rows must be 16-byte aligned");
+    ESP_REQUIRE(maxm >= R && maxu >= 1, ESP_ERR_INVALID, "route_group: members must hold R entries an expert");
+    const int C = E + has;
+    int rc;
+    if (x_dtype == ESP_DTYPE_BF16)
+        rc = launch(route_kernel<__nv_bfloat16>, dim3(C), dim3(RT), 0, stream, true,
+                    static_cast<const __nv_bfloat16*>(x), x_stride, R, H, static_cast<const __nv_bfloat16*>(gate), E,
+                    static_cast<const __nv_bfloat16*>(sgate), k, shared_id, logits, counter, pick_out, wts_out, uids,
+                    ucount, members, maxm, maxu);
+    else
+        rc = launch(route_kernel<__half>, dim3(C), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
+                    R, H, static_cast<const __half*>(gate), E, static_cast<const __half*>(sgate), k, shared_id, logits,
+                    counter, pick_out, wts_out, uids, ucount, members, maxm, maxu);
+    if (rc) return rc;
+    return ok();
+}
+
+int esp_group(const int* pick, int R, int slots, int E, int* uids, int* ucount, int* members, int maxm, int maxu,
+              void* stream) {
+    ESP_REQUIRE(pick && uids && ucount && members, ESP_ERR_INVALID, "group: null pointer");
+    ESP_REQUIRE(E >= 1 && E <= MAX_E, ESP_ERR_INVALID, "too many experts for the grouping kernel");
+    ESP_REQUIRE(slots >= 1 && slots <= 32, ESP_ERR_INVALID, "at most 32 slots a row");
+    ESP_REQUIRE(R >= 1 && R * slots <= MAX_PICKS, ESP_ERR_INVALID, "grouping window too large");
+    ESP_REQUIRE(maxm >= 1 && maxu >= 1, ESP_ERR_INVALID, "members too small");
+    if (int rc = launch(group_kernel, dim3(1), dim3(RT), 0, stream, true, pick, R * slots, slots, E, uids, ucount,
+                        members, maxm, maxu))
+        return rc;
+    return ok();
+}
+
+int esp_group_shared(const int* pick_in, const float* wts_in, const void* x, int x_dtype, long long x_stride, int H,
+                     const void* gate_w, int shared_id, int* pick_out, float* wts_out, int* uids, int* ucount,
+                     int* members, int R, int slots_in, int E, int maxm, int maxu, void* stream) {
+    ESP_REQUIRE(pick_in && wts_in && x && pick_out && wts_out && uids && ucount && members, ESP_ERR_INVALID,
+                "group_shared: null pointer");
+    ESP_REQUIRE(E >= 1 && E <= MAX_E, ESP_ERR_INVALID, "too many experts for the grouping kernel");
+    const int slots = slots_in + (shared_id >= 0);
+    ESP_REQUIRE(slots <= 32 && R >= 1 && R * slots <= MAX_PICKS, ESP_ERR_INVALID, "grouping window too large");
+    ESP_REQUIRE(shared_id < 0 || gate_w, ESP_ERR_INVALID, "a shared slot needs its gate weight");
+    ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "x: bf16/fp16");
+    int rc;
+    if (x_dtype == ESP_DTYPE_BF16)
+        rc = launch(group_shared_kernel<__nv_bfloat16>, dim3(1), dim3(RT), 0, stream, true, pick_in, wts_in,
+                    static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(gate_w), H,
+                    shared_id, pick_out, wts_out, uids, ucount, members, R, slots_in, E, maxm, maxu);
+    else
+        rc = launch(group_shared_kernel<__half>, dim3(1), dim3(RT), 0, stream, true, pick_in, wts_in,
+                    static_cast<const __half*>(x), x_stride, static_cast<const __half*>(gate_w), H, shared_id, pick_out,
+                    wts_out, uids, ucount, members, R, slots_in, E, maxm, maxu);
+    if (rc) return rc;
+    return ok();
+}
+
+}  // extern "C"
