@@ -129,11 +129,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls (a try_wait may suspend briefly): about a second, never forever
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
+constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;   // a wait gives up after 0.2 s of wall time, never hangs
+
+// Wait for the phase of `parity` to complete. Gives up after WAIT_NS (time, not polls: a suspended try_wait may sleep),
+// records ESP_ERR_TIMEOUT and returns false. Once any wait of this file's kernels has timed out, later waits that do
+// not complete at once fail at once too, so a broken pipeline ends in one WAIT_NS, not one a stage.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > WAIT_NS) break;
+    }
     report(ESP_ERR_TIMEOUT);
     return false;
 }

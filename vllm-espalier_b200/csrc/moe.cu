@@ -129,13 +129,19 @@ __device__ __forceinline__ void stage_units(const uint32_t* st, const uint32_t* 
                                             int slice_w, int grp, int wl, int lane, int ntg, float (&acc)[2][NTG][4]) {
     const int g = lane >> 2, t = lane & 3;
     constexpr int TW = 8 * K;
-    for (int jj = j0 + ((j0 & 1) != grp ? 1 : 0); jj < j1; jj += 2) {
+    // this group's units are every other one; consecutive ones alternate between two accumulator sets (static indices,
+    // so the accumulators stay in registers)
+    auto unit = [&](int jj, float (&ac)[NTG][4]) {
         uint32_t a[4];
         decode_a<CB, K>(st + jj * unit_w + wl * TW, lane, a);
         const uint32_t* xs = xs0 + jj * slice_w;
 #pragma unroll
         for (int q = 0; q < NTG; ++q)
-            if (q < ntg) mma16816(acc[(jj >> 1) & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(8 * NTG + 8 * q + g) * 4 + t]);
+            if (q < ntg) mma16816(ac[q], a, xs[(8 * q + g) * 4 + t], xs[(8 * NTG + 8 * q + g) * 4 + t]);
+    };
+    for (int jj = j0 + ((j0 & 1) != grp ? 1 : 0); jj < j1; jj += 4) {
+        unit(jj, acc[0]);
+        if (jj + 2 < j1) unit(jj + 2, acc[1]);
     }
 }
 
@@ -155,6 +161,54 @@ __device__ __forceinline__ void dispatch_units(int cb, int K, const uint32_t* st
     }
 }
 
+// The gate/up epilogue of one member row's 4 columns of this lane (experts.cu:120-162, act_mode 1): sums times the
+// codebook steps, H, * h * svh, silu(g) * u, * suh_d (never contracted into the butterfly), H, * h -> fp16 xd.
+__device__ __forceinline__ void swiglu_store(const GroupedParams& p, int e, int n0, int pm, float cg, float cu,
+                                             float (&gv)[4], float (&uv)[4], int lane) {
+    const __half* svg = p.svh_g + (size_t)e * p.N + n0;
+    const __half* svu = p.svh_u + (size_t)e * p.N + n0;
+    const __half* sud = p.suh_d + (size_t)e * p.N + n0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        gv[j] *= cg;
+        uv[j] *= cu;
+    }
+    fwht128(gv, lane);
+    fwht128(uv, lane);
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float gg = gv[j] * HAD_SCALE * __half2float(svg[j]);
+        const float uu = uv[j] * HAD_SCALE * __half2float(svu[j]);
+        const float act = gg / (1.f + expf(-gg)) * uu;
+        v[j] = __fmul_rn(act, __half2float(sud[j]));
+    }
+    fwht128(v, lane);
+    const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
+    const __half2 bq = __floats2half2_rn(v[2] * HAD_SCALE, v[3] * HAD_SCALE);
+    uint2 uo;
+    uo.x = *reinterpret_cast<const uint32_t*>(&a);
+    uo.y = *reinterpret_cast<const uint32_t*>(&bq);
+    *reinterpret_cast<uint2*>(p.xd + (size_t)pm * p.N + n0) = uo;
+}
+
+// Per work item descriptor, written into shared memory by the producer and read by the consumers.
+struct ItemDesc {
+    int e, b, split, mat0, nmats, kt0, nkt, nm;
+    int cb0, K0, cb1, K1;
+    int rows[32];          // slot index p of each member
+};
+constexpr int NDESC = 8;   // descriptor ring (an item spans at least one stage; the ring is 4 stages deep)
+constexpr int MAX_PEND = 1024;     // deferred arrivals a CTA (items a CTA x members an item)
+
+// Work item `it` of MODE: (expert position u, block b, z); z = split (fused modes) or mat * S + split (MODE_Z).
+__device__ __forceinline__ void item_coords(const GroupedParams& p, int it, int NB, int NZ, int& u, int& b, int& z) {
+    u = it / (NB * NZ);
+    const int r = it - u * NB * NZ;
+    b = r / NZ;
+    z = r - b * NZ;
+}
+
 template <int NTG, int KCAP>
 __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_constant__ GroupedParams p) {
     constexpr int MP = 8 * NTG;
@@ -165,85 +219,105 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     float* red = reinterpret_cast<float*>(smem + (size_t)GSTAGES * STAGE_W);       // [2][MP][GRED]
     uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * MP * GRED);
     uint64_t* empty = full + GSTAGES;
-    __shared__ int s_rows[32];        // slot index p of each member
-    __shared__ int s_last;
+    __shared__ ItemDesc desc[NDESC];
+    __shared__ int s_pend[MAX_PEND][2];      // deferred arrivals: (counter index, item or row code)
+    __shared__ int s_npend;
+    __shared__ int s_last[MAX_PEND];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NB = p.N / 128;
-    const int u = blockIdx.x;
+    const int NZ = p.mode == MODE_Z ? p.mats * p.S : p.S;
+    const int KT = p.K / 16;
     pdl_launch_dependents();
     pdl_wait();
-    if (u >= p.ucount[0]) return;                    // grid is sized for the most experts a window can touch
-
-    CtaWork w;
-    w.e = p.uids[u];
-    w.b = blockIdx.y;
-    if (p.mode == MODE_Z) {
-        w.split = blockIdx.z % p.S;
-        w.mat0 = blockIdx.z / p.S;
-        w.nmats = 1;
-    } else {
-        w.split = blockIdx.z;
-        w.mat0 = 0;
-        w.nmats = p.mats;
-    }
-    const int KT = p.K / 16;
-    w.kt0 = w.split * KT / p.S;
-    w.nkt = (w.split + 1) * KT / p.S - w.kt0;
-    if (threadIdx.x < 32) {
-        const int code = threadIdx.x < p.maxm ? p.members[u * p.maxm + threadIdx.x] : -1;
-        s_rows[threadIdx.x] = code >= 0 ? (code >> 5) * p.slots + (code & 31) : -1;
-    }
-    int cbs[2], Ks[2];
-    for (int m = 0; m < 2; ++m) {
-        const int mm = min(w.mat0 + m, p.mats - 1);
-        cbs[m] = p.cb[mm][w.e];
-        Ks[m] = p.k2[mm][w.e] / 2;
-    }
+    const int n_items = p.ucount[0] * NB * NZ;         // grid: one CTA an SM, items round robin
     if (threadIdx.x == 0) {
         for (int i = 0; i < GSTAGES; ++i) {
-            mbar_init(&full[i], 32);
+            mbar_init(&full[i], 33);                   // 32 copy arrivals + the producer's release of descriptors
             mbar_init(&empty[i], GWARPS);
         }
+        s_npend = 0;
         fence_mbar_init();
     }
+    // a zeroed descriptor ring: a consumer that reads a slot after a timed-out wait sees an empty item, never garbage
+    for (int i = threadIdx.x; i < NDESC * (int)(sizeof(ItemDesc) / 4); i += GTHREADS)
+        reinterpret_cast<int*>(desc)[i] = 0;
     __syncthreads();
-    int nm = 0;
-    while (nm < 32 && s_rows[nm] >= 0) ++nm;           // members come first
-    w.nm = nm;
-    const int ntg = (nm + 7) / 8;
-    const int n = w.nmats * w.nkt;                     // units: matrix-major, then k-tile
-    const int nst = (n + GUPS - 1) / GUPS;
-
-    if (warp == GWARPS) {   // ---------------- producer: 16-byte async copies from all lanes ----------------
-        auto fill = [&](int i, int slot) {
-            uint32_t* st = smem + (size_t)slot * STAGE_W;
-            const int m0 = min(GUPS, n - i * GUPS);
-            for (int j = 0; j < m0; ++j) {
-                const int un = i * GUPS + j, mi = un / w.nkt, kt = w.kt0 + un % w.nkt;
-                const int mat = w.mat0 + mi;
-                const int TW = 8 * Ks[mi];
-                const uint32_t* T = reinterpret_cast<const uint32_t*>(p.tp[mat][w.e]);
-                const uint32_t* src = T + ((size_t)kt * (p.N / 16) + (size_t)w.b * 8) * TW;
-                for (int q = lane; q < 2 * TW; q += 32) cp_async16(st + j * UNIT_WMAX + q * 4, src + q * 4);
-                // member slice of k-tile kt: [h][m][8 halves] from rows X[p_m][16 kt + 8 h ...]
-                const __half* X = p.X[mat];
-                for (int q = lane; q < 2 * nm; q += 32) {
-                    const int m = q >> 1, h = q & 1;
-                    cp_async16(st + GUPS * UNIT_WMAX + j * SLICE_W + (h * MP + m) * 4,
-                               X + (size_t)s_rows[m] * p.K + kt * 16 + h * 8);
-                }
+    if (p.mode == MODE_DOWN && blockIdx.x == 0 && warp < GWARPS) {   // rows without a valid slot get zeros
+        const int rows = p.P / p.slots;
+        for (int r = warp; r < rows; r += GWARPS) {
+            bool any = false;
+            for (int j = 0; j < p.slots; ++j) {
+                const int e2 = p.pick[r * p.slots + j];
+                any |= e2 >= 0 && e2 < p.E;
             }
-            cp_async_arrive(&full[slot]);
-        };
-        const int pre = min(nst, GSTAGES);
-        for (int i = 0; i < pre; ++i) fill(i, i);
-        for (int i = GSTAGES, slot = 0, phase = 0; i < nst; ++i) {
-            if (!mbar_wait(&empty[slot], phase)) return;
-            fill(i, slot);
-            if (++slot == GSTAGES) {
-                slot = 0;
-                phase ^= 1;
+            if (any) continue;
+            const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int n0 = 4 * lane; n0 < p.N; n0 += 128) {
+                store4(p.out, p.out_dtype, (size_t)r * p.N + n0, zero);
+                if (p.out_shared) store4(p.out_shared, p.out_dtype, (size_t)r * p.N + n0, zero);
+            }
+        }
+    }
+    if ((int)blockIdx.x >= n_items) return;
+
+    if (warp == GWARPS) {   // ---------------- producer ----------------
+        int slot = 0, phase = 0, nstage = 0, di = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
+            int u, b, z;
+            item_coords(p, it, NB, NZ, u, b, z);
+            ItemDesc& d = desc[di];
+            const int e = p.uids[u];
+            const int split = p.mode == MODE_Z ? z % p.S : z;
+            const int mat0 = p.mode == MODE_Z ? z / p.S : 0;
+            const int nmats = p.mode == MODE_Z ? 1 : p.mats;
+            const int mmB = min(mat0 + 1, p.mats - 1);
+            const int code = lane < p.maxm ? p.members[u * p.maxm + lane] : -1;
+            const int row = code >= 0 ? (code >> 5) * p.slots + (code & 31) : -1;
+            const int nm = __popc(__ballot_sync(0xffffffffu, row >= 0));
+            const int cb0 = p.cb[mat0][e], cb1 = p.cb[mmB][e];
+            const int K0 = p.k2[mat0][e] / 2, K1 = p.k2[mmB][e] / 2;
+            const uint32_t* T0 = reinterpret_cast<const uint32_t*>(p.tp[mat0][e]);
+            const uint32_t* T1 = reinterpret_cast<const uint32_t*>(p.tp[mmB][e]);
+            const __half* X0 = p.X[mat0];
+            const __half* X1 = p.X[mmB];
+            const int kt0 = split * KT / p.S, nkt = (split + 1) * KT / p.S - kt0;
+            // the descriptor slot was last read by the consumers' epilogue of item (this - NDESC), which ended before
+            // they released the stage this item's first units need
+            d.rows[lane] = row;
+            if (lane == 0) {
+                d.e = e; d.b = b; d.split = split; d.mat0 = mat0; d.nmats = nmats; d.kt0 = kt0; d.nkt = nkt;
+                d.nm = nm; d.cb0 = cb0; d.K0 = K0; d.cb1 = cb1; d.K1 = K1;
+            }
+            __syncwarp();
+            const int n = nmats * nkt;
+            int mi = 0, kt = kt0;
+            for (int i0 = 0; i0 < n; i0 += GUPS) {
+                if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
+                uint32_t* st = smem + (size_t)slot * STAGE_W;
+                const int m0 = min(GUPS, n - i0);
+                for (int j = 0; j < m0; ++j) {
+                    const int TW = 8 * (mi ? K1 : K0);
+                    const uint32_t* src = (mi ? T1 : T0) + ((size_t)kt * (p.N / 16) + (size_t)b * 8) * TW;
+                    for (int q = lane; q < 2 * TW; q += 32) cp_async16(st + j * UNIT_WMAX + q * 4, src + q * 4);
+                    const __half* X = mi ? X1 : X0;
+                    for (int q = lane; q < 2 * nm; q += 32) {
+                        const int m = q >> 1, h = q & 1;
+                        cp_async16(st + GUPS * UNIT_WMAX + j * SLICE_W + (h * MP + m) * 4,
+                                   X + (size_t)d.rows[m] * p.K + kt * 16 + h * 8);
+                    }
+                    if (++kt == kt0 + nkt) {
+                        kt = kt0;
+                        mi = 1;
+                    }
+                }
+                cp_async_arrive(&full[slot]);
+                if (lane == 0) mbar_arrive(&full[slot]);      // releases this item's descriptor with the stage
+                ++nstage;
+                if (++slot == GSTAGES) {
+                    slot = 0;
+                    phase ^= 1;
+                }
             }
         }
         return;
@@ -253,187 +327,190 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     const int grp = warp >> 3, wl = warp & 7;
     const int g = lane >> 2, t = lane & 3;
     constexpr int CT = GWARPS * 32;
-    float acc[2][2][NTG][4];          // [matrix][even/odd unit][token group][4]
+    int slot = 0, phase = 0, di = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
+        float acc[2][2][NTG][4];      // [matrix][even/odd unit][token group][4]
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+        for (int m = 0; m < 2; ++m)
 #pragma unroll
-        for (int e2 = 0; e2 < 2; ++e2)
+            for (int e2 = 0; e2 < 2; ++e2)
 #pragma unroll
-            for (int q = 0; q < NTG; ++q) acc[m][e2][q][0] = acc[m][e2][q][1] = acc[m][e2][q][2] = acc[m][e2][q][3] = 0.f;
-
-    for (int i = 0, slot = 0, phase = 0; i < nst; ++i) {
-        mbar_wait(&full[slot], phase);
-        const uint32_t* st = smem + (size_t)slot * STAGE_W;
-        const uint32_t* xs0 = st + GUPS * UNIT_WMAX;
-        const int m0 = min(GUPS, n - i * GUPS);
-        // units of this stage by matrix: [u0, u0 + m0) splits at the matrix boundary
-        const int un0 = i * GUPS;
-        const int split_at = min(m0, max(0, w.nkt - un0));     // units of matrix 0 in this stage
-        if (split_at > 0) dispatch_units<NTG, KCAP>(cbs[0], Ks[0], st, xs0, 0, split_at, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[0]);
-        if (m0 > split_at) dispatch_units<NTG, KCAP>(cbs[1], Ks[1], st, xs0, split_at, m0, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[1]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (++slot == GSTAGES) {
-            slot = 0;
-            phase ^= 1;
+                for (int q = 0; q < NTG; ++q) acc[m][e2][q][0] = acc[m][e2][q][1] = acc[m][e2][q][2] = acc[m][e2][q][3] = 0.f;
+        const ItemDesc* d = &desc[di];
+        int nkt = 0, nmats = 0, ntg = 0, cb0 = 0, K0 = 0, cb1 = 0, K1 = 0;
+        for (int i0 = 0;; i0 += GUPS) {
+            mbar_wait(&full[slot], phase);
+            if (i0 == 0) {   // the descriptor is published with the item's first stage
+                nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
+                cb0 = d->cb0; K0 = d->K0; cb1 = d->cb1; K1 = d->K1;
+            }
+            const int n = nmats * nkt;
+            const uint32_t* st = smem + (size_t)slot * STAGE_W;
+            const uint32_t* xs0 = st + GUPS * UNIT_WMAX;
+            const int m0 = min(GUPS, n - i0);
+            const int split_at = min(m0, max(0, nkt - i0));     // units of matrix 0 in this stage
+            if (split_at > 0)
+                dispatch_units<NTG, KCAP>(cb0, K0, st, xs0, 0, split_at, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[0]);
+            if (m0 > split_at)
+                dispatch_units<NTG, KCAP>(cb1, K1, st, xs0, split_at, m0, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[1]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == GSTAGES) {
+                slot = 0;
+                phase ^= 1;
+            }
+            if (i0 + GUPS >= n) break;
         }
-    }
 
-    // ---- the CTA's sums: group 0 then group 1, even + odd units, into red[matrix][member][column] ----
-    const int col = wl * 16 + g;
-    for (int gi = 0; gi < 2; ++gi) {
-        if (gi == grp)
-            for (int m = 0; m < w.nmats; ++m)
+        // ---- the item's sums: group 0 then group 1, even + odd units, into red[matrix][member][column] ----
+        const int col = wl * 16 + g;
+        for (int gi = 0; gi < 2; ++gi) {
+            if (gi == grp)
 #pragma unroll
-                for (int q = 0; q < NTG; ++q) {
-                    const int r0 = 8 * q + 2 * t;
-                    float* rr = red + ((size_t)m * MP + r0) * GRED + col;
-                    const float v0 = acc[m][0][q][0] + acc[m][1][q][0], v1 = acc[m][0][q][1] + acc[m][1][q][1];
-                    const float v2 = acc[m][0][q][2] + acc[m][1][q][2], v3 = acc[m][0][q][3] + acc[m][1][q][3];
-                    if (gi == 0) {
-                        rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
-                    } else {
-                        rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int q = 0; q < NTG; ++q) {
+                        if (m >= nmats) continue;
+                        const int r0 = 8 * q + 2 * t;
+                        float* rr = red + ((size_t)m * MP + r0) * GRED + col;
+                        const float v0 = acc[m][0][q][0] + acc[m][1][q][0], v1 = acc[m][0][q][1] + acc[m][1][q][1];
+                        const float v2 = acc[m][0][q][2] + acc[m][1][q][2], v3 = acc[m][0][q][3] + acc[m][1][q][3];
+                        if (gi == 0) {
+                            rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
+                        } else {
+                            rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
+                        }
                     }
-                }
-        named_sync(1, CT);
-    }
-
-    const int n0 = w.b * 128 + 4 * lane;               // this lane's 4 output columns
-    if (p.mode == MODE_Z) {   // sums of the exact weights: the kernel form times its codebook step
-        const float c0 = cb_step(cbs[0]);
-        for (int m = warp; m < nm; m += GWARPS) {
-            float4 v = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
-            v.x *= c0; v.y *= c0; v.z *= c0; v.w *= c0;
-            *reinterpret_cast<float4*>(p.Z + (((size_t)w.mat0 * p.S + w.split) * p.P + s_rows[m]) * p.N + n0) = v;
+            named_sync(1, CT);
         }
-        return;
-    }
+        const int e = d->e, b = d->b, nm = d->nm;
+        const int n0 = b * 128 + 4 * lane;
+        int u, bb, z;
+        item_coords(p, it, NB, NZ, u, bb, z);
 
-    if (p.mode == MODE_GATEUP) {
-        bool finish = true;
-        if (p.S > 1) {   // partials of this slice; the last CTA of (expert, block) adds the slices in order
+        if (p.mode == MODE_Z) {   // sums of the exact weights: the kernel form times its codebook step
+            const float c0 = cb_step(cb0);
+            for (int m = warp; m < nm; m += GWARPS) {
+                float4 v = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                v.x *= c0; v.y *= c0; v.z *= c0; v.w *= c0;
+                *reinterpret_cast<float4*>(p.Z + (((size_t)d->mat0 * p.S + d->split) * p.P + d->rows[m]) * p.N + n0) = v;
+            }
+        } else if (p.mode == MODE_GATEUP && p.S > 1) {   // slice partials; arrivals after the last item
             for (int m = warp; m < nm; m += GWARPS)
                 for (int mi = 0; mi < 2; ++mi)
-                    *reinterpret_cast<float4*>(p.Z + (((size_t)mi * p.S + w.split) * p.P + s_rows[m]) * p.N + n0) =
+                    *reinterpret_cast<float4*>(p.Z + (((size_t)mi * p.S + d->split) * p.P + d->rows[m]) * p.N + n0) =
                         *reinterpret_cast<const float4*>(red + ((size_t)mi * MP + m) * GRED + 4 * lane);
-            named_sync(1, CT);
             if (threadIdx.x == 0) {
-                fence_acq_rel_gpu();
-                s_last = atomicAdd(&p.counters[u * NB + w.b], 1) == p.S - 1;
-                fence_acq_rel_gpu();
+                s_pend[s_npend][0] = u * NB + b;
+                s_pend[s_npend][1] = it;
+                ++s_npend;
+            }
+        } else if (p.mode == MODE_GATEUP) {   // whole K in this item: the epilogue now
+            for (int m = warp; m < nm; m += GWARPS) {
+                const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                const float4 c4 = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
+                float gv[4] = {a.x, a.y, a.z, a.w}, uv[4] = {c4.x, c4.y, c4.z, c4.w};
+                swiglu_store(p, e, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
+            }
+        } else {   // MODE_DOWN: y for this block; row arrivals after the last item
+            const float cd = cb_step(cb0);
+            const __half* svd = p.svh_d + (size_t)e * p.N + n0;
+            for (int m = warp; m < nm; m += GWARPS) {
+                const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                float v[4] = {a.x * cd, a.y * cd, a.z * cd, a.w * cd};
+                fwht128(v, lane);
+                float4 o;
+                o.x = v[0] * HAD_SCALE * __half2float(svd[0]);
+                o.y = v[1] * HAD_SCALE * __half2float(svd[1]);
+                o.z = v[2] * HAD_SCALE * __half2float(svd[2]);
+                o.w = v[3] * HAD_SCALE * __half2float(svd[3]);
+                *reinterpret_cast<float4*>(p.y + (size_t)d->rows[m] * p.N + n0) = o;
+            }
+            if (threadIdx.x < nm) {
+                const int r = d->rows[threadIdx.x] / p.slots;
+                s_pend[s_npend + threadIdx.x][0] = r * NB + b;
+                s_pend[s_npend + threadIdx.x][1] = r * 256 + b;
             }
             named_sync(1, CT);
-            finish = s_last;
+            if (threadIdx.x == 0) s_npend += nm;
         }
-        if (!finish) return;
-        const __half* svg = p.svh_g + (size_t)w.e * p.N + n0;
-        const __half* svu = p.svh_u + (size_t)w.e * p.N + n0;
-        const __half* sud = p.suh_d + (size_t)w.e * p.N + n0;
-        for (int m = warp; m < nm; m += GWARPS) {
-            float gv[4], uv[4];
-            if (p.S > 1) {
-                float4 sg = make_float4(0.f, 0.f, 0.f, 0.f), su = sg;
-                for (int s = 0; s < p.S; ++s) {
-                    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)s * p.P + s_rows[m]) * p.N + n0));
-                    const float4 b = __ldcg(reinterpret_cast<const float4*>(p.Z + (((size_t)p.S + s) * p.P + s_rows[m]) * p.N + n0));
-                    sg.x += a.x; sg.y += a.y; sg.z += a.z; sg.w += a.w;
-                    su.x += b.x; su.y += b.y; su.z += b.z; su.w += b.w;
-                }
-                gv[0] = sg.x; gv[1] = sg.y; gv[2] = sg.z; gv[3] = sg.w;
-                uv[0] = su.x; uv[1] = su.y; uv[2] = su.z; uv[3] = su.w;
-            } else {
-                const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
-                const float4 b = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
-                gv[0] = a.x; gv[1] = a.y; gv[2] = a.z; gv[3] = a.w;
-                uv[0] = b.x; uv[1] = b.y; uv[2] = b.z; uv[3] = b.w;
-            }
-            // the codebook step of each matrix (its kernel form) before the reference's epilogue arithmetic
-            const float cg = cb_step(cbs[0]), cu = cb_step(cbs[1]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                gv[j] *= cg;
-                uv[j] *= cu;
-            }
-            fwht128(gv, lane);
-            fwht128(uv, lane);
-            float v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float gg = gv[j] * HAD_SCALE * __half2float(svg[j]);
-                const float uu = uv[j] * HAD_SCALE * __half2float(svu[j]);
-                const float act = gg / (1.f + expf(-gg)) * uu;
-                v[j] = __fmul_rn(act, __half2float(sud[j]));      // never contracted into the butterfly
-            }
-            fwht128(v, lane);
-            __half* o = p.xd + (size_t)s_rows[m] * p.N + n0;
-            const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
-            const __half2 bq = __floats2half2_rn(v[2] * HAD_SCALE, v[3] * HAD_SCALE);
-            uint2 uo;
-            uo.x = *reinterpret_cast<const uint32_t*>(&a);
-            uo.y = *reinterpret_cast<const uint32_t*>(&bq);
-            *reinterpret_cast<uint2*>(o) = uo;
-        }
-        if (p.S > 1 && threadIdx.x == 0) p.counters[u * NB + w.b] = 0;
-        return;
+        named_sync(1, CT);   // red and the descriptor are free for the next item
     }
 
-    // ---- MODE_DOWN: y[p] for this block, then the combine of every row whose slots are all done ----
-    const float cd = cb_step(cbs[0]);
-    const __half* svd = p.svh_d + (size_t)w.e * p.N + n0;
-    for (int m = warp; m < nm; m += GWARPS) {
-        const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
-        float v[4] = {a.x * cd, a.y * cd, a.z * cd, a.w * cd};
-        fwht128(v, lane);
-        float4 o;
-        o.x = v[0] * HAD_SCALE * __half2float(svd[0]);
-        o.y = v[1] * HAD_SCALE * __half2float(svd[1]);
-        o.z = v[2] * HAD_SCALE * __half2float(svd[2]);
-        o.w = v[3] * HAD_SCALE * __half2float(svd[3]);
-        *reinterpret_cast<float4*>(p.y + (size_t)s_rows[m] * p.N + n0) = o;
-    }
+    // ---------------- deferred arrivals: the last arriver finishes ----------------
     named_sync(1, CT);
-    __shared__ int s_lastrow[32];
-    if (threadIdx.x < nm) {
-        const int pp = s_rows[threadIdx.x], r = pp / p.slots;
-        int valid = 0;
-        for (int j = 0; j < p.slots; ++j) {
-            const int e = p.pick[r * p.slots + j];
-            valid += e >= 0 && e < p.E;
+    const int np = s_npend;
+    if (np == 0) return;
+    for (int i = threadIdx.x; i < np; i += CT) {
+        int target;
+        if (p.mode == MODE_GATEUP) {
+            target = p.S;
+        } else {
+            const int r = s_pend[i][1] >> 8;
+            target = 0;
+            for (int j = 0; j < p.slots; ++j) {
+                const int e2 = p.pick[r * p.slots + j];
+                target += e2 >= 0 && e2 < p.E;
+            }
         }
         fence_acq_rel_gpu();
-        s_lastrow[threadIdx.x] = atomicAdd(&p.counters[r * NB + w.b], 1) == valid - 1;
+        s_last[i] = atomicAdd(&p.counters[s_pend[i][0]], 1) == target - 1;
         fence_acq_rel_gpu();
     }
     named_sync(1, CT);
-    for (int m = warp; m < nm; m += GWARPS) {
-        if (!s_lastrow[m]) continue;
-        const int r = s_rows[m] / p.slots;
-        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < p.n_routed; ++j) {
-            const int q = r * p.slots + j;
-            const int e = p.pick[q];
-            if (e < 0 || e >= p.E) continue;
-            const float wq = p.wts[q];
-            const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.N + n0));
-            acc4[0] = fmaf(wq, yv.x, acc4[0]);
-            acc4[1] = fmaf(wq, yv.y, acc4[1]);
-            acc4[2] = fmaf(wq, yv.z, acc4[2]);
-            acc4[3] = fmaf(wq, yv.w, acc4[3]);
-        }
-        store4(p.out, p.out_dtype, (size_t)r * p.N + n0, acc4);
-        if (p.out_shared && p.n_routed < p.slots) {
-            const int q = r * p.slots + p.n_routed;
-            const int e = p.pick[q];
-            float sv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (e >= 0 && e < p.E) {
+    for (int pi = 0; pi < np; ++pi) {
+        if (!s_last[pi]) continue;
+        if (p.mode == MODE_GATEUP) {   // add the S slices in order, then the SwiGLU epilogue
+            int u, b, z;
+            item_coords(p, s_pend[pi][1], NB, NZ, u, b, z);
+            const int e = p.uids[u];
+            const float cg = cb_step(p.cb[0][e]), cu = cb_step(p.cb[1 % p.mats][e]);
+            const int n0 = b * 128 + 4 * lane;
+            for (int m = warp; m < p.maxm; m += GWARPS) {
+                const int code = p.members[u * p.maxm + m];
+                if (code < 0) continue;
+                const int pm = (code >> 5) * p.slots + (code & 31);
+                float4 sg = make_float4(0.f, 0.f, 0.f, 0.f), su = sg;
+                for (int s2 = 0; s2 < p.S; ++s2) {
+                    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)s2 * p.P + pm) * p.N + n0));
+                    const float4 c4 = __ldcg(reinterpret_cast<const float4*>(p.Z + (((size_t)p.S + s2) * p.P + pm) * p.N + n0));
+                    sg.x += a.x; sg.y += a.y; sg.z += a.z; sg.w += a.w;
+                    su.x += c4.x; su.y += c4.y; su.z += c4.z; su.w += c4.w;
+                }
+                float gv[4] = {sg.x, sg.y, sg.z, sg.w}, uv[4] = {su.x, su.y, su.z, su.w};
+                swiglu_store(p, e, n0, pm, cg, cu, gv, uv, lane);
+            }
+            if (threadIdx.x == 0) p.counters[s_pend[pi][0]] = 0;
+        } else {                        // MODE_DOWN: combine the row's slots in slot order
+            const int r = s_pend[pi][1] >> 8, b = s_pend[pi][1] & 255;
+            if (warp != pi % GWARPS) continue;
+            const int n0 = b * 128 + 4 * lane;
+            float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int j = 0; j < p.n_routed; ++j) {
+                const int q = r * p.slots + j;
+                const int e2 = p.pick[q];
+                if (e2 < 0 || e2 >= p.E) continue;
                 const float wq = p.wts[q];
                 const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.N + n0));
-                sv[0] = wq * yv.x; sv[1] = wq * yv.y; sv[2] = wq * yv.z; sv[3] = wq * yv.w;
+                acc4[0] = fmaf(wq, yv.x, acc4[0]);
+                acc4[1] = fmaf(wq, yv.y, acc4[1]);
+                acc4[2] = fmaf(wq, yv.z, acc4[2]);
+                acc4[3] = fmaf(wq, yv.w, acc4[3]);
             }
-            store4(p.out_shared, p.out_dtype, (size_t)r * p.N + n0, sv);
+            store4(p.out, p.out_dtype, (size_t)r * p.N + n0, acc4);
+            if (p.out_shared && p.n_routed < p.slots) {
+                const int q = r * p.slots + p.n_routed;
+                const int e2 = p.pick[q];
+                float sv[4] = {0.f, 0.f, 0.f, 0.f};
+                if (e2 >= 0 && e2 < p.E) {
+                    const float wq = p.wts[q];
+                    const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.N + n0));
+                    sv[0] = wq * yv.x; sv[1] = wq * yv.y; sv[2] = wq * yv.z; sv[3] = wq * yv.w;
+                }
+                store4(p.out_shared, p.out_dtype, (size_t)r * p.N + n0, sv);
+            }
+            if (lane == 0) p.counters[s_pend[pi][0]] = 0;
         }
-        if (lane == 0) p.counters[r * NB + w.b] = 0;
     }
 }
 
@@ -575,7 +652,12 @@ int launch_grouped_t(const GroupedParams& p, dim3 grid, void* stream) {
 }
 
 int launch_grouped(const GroupedParams& p, int ntg, int kmax, int maxu, void* stream) {
-    const dim3 grid((unsigned)maxu, (unsigned)(p.N / 128), (unsigned)(p.mode == MODE_Z ? p.mats * p.S : p.S));
+    // persistent: one CTA an SM (never more than the most items a window can have)
+    const long long most = (long long)maxu * (p.N / 128) * (p.mode == MODE_Z ? p.mats * p.S : p.S);
+    const dim3 grid((unsigned)std::min<long long>(device_sms(), most));
+    const long long per_cta = (most + grid.x - 1) / grid.x;
+    ESP_REQUIRE(per_cta * (p.mode == MODE_DOWN ? p.maxm : 1) <= MAX_PEND, ESP_ERR_INVALID,
+                "grouped: %lld items a CTA exceed the deferred-arrival table", per_cta);
 #define ESP_G(N_)                                                                                   \
     return kmax <= 4 ? launch_grouped_t<N_, 4>(p, grid, stream) : launch_grouped_t<N_, 8>(p, grid, stream);
     switch (ntg) {
@@ -695,7 +777,9 @@ int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const
                     cb_host,
                 ESP_ERR_INVALID, "moe_down: null pointer");
     ESP_REQUIRE(D % 128 == 0 && I % 128 == 0, ESP_ERR_INVALID, "moe_down: shapes");
-    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && n_routed <= slots, ESP_ERR_INVALID, "moe_down: limits");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && slots >= 1 && slots <= 32 && n_routed <= slots &&
+                    D / 128 <= 256,
+                ESP_ERR_INVALID, "moe_down: limits (32 members, 32 slots, D <= 32768)");
     ESP_REQUIRE(out_dtype >= 0 && out_dtype <= 2, ESP_ERR_INVALID, "moe_down: dtype");
     int kmax = 0;
     if (int rc = check_tables(k2_host, cb_host, E, kmax)) return rc;

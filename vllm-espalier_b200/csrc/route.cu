@@ -13,7 +13,7 @@
 // to far below bf16 resolution, so they equal the correctly rounded logits' choice. Top-k compares bf16 logit values
 // (exp is monotone), so the choice does not depend on the exponential's last bit.
 //
-// B200 layout: one CTA a logit column (E experts + the shared gate), 8 warps over the rows; the last CTA to arrive
+// B200 layout: a warp a logit column (E experts + the shared gate), all of its loads in flight at once; the last CTA to arrive
 // (acq_rel counter) does the per-row selection (a warp a row) and the grouping, then resets the counter.
 #include <cuda_runtime.h>
 
@@ -40,15 +40,33 @@ template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 
-// fp64 logit of one row against one weight row, in the documented order; every lane returns the full sum.
+// fp64 logit of one row against one weight row, in the documented order; every lane returns the full sum. All of the
+// lane's loads are issued before the first fused multiply-add (H <= 2048: at most 8 chunks of 8 a lane).
 template <typename T>
 __device__ __forceinline__ double logit64(const T* __restrict__ x, const T* __restrict__ w, int H, int lane) {
+    constexpr int MAXC = 8;
+    uint4 ux[MAXC], uw[MAXC];
+    const int nc = (H - 8 * lane + 255) / 256;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+        if (i < nc) {
+            ux[i] = *reinterpret_cast<const uint4*>(x + 8 * lane + 256 * i);
+            uw[i] = *reinterpret_cast<const uint4*>(w + 8 * lane + 256 * i);
+        }
     double acc = 0.0;
-    for (int j0 = 8 * lane; j0 < H; j0 += 256) {
-        const uint4 ux = *reinterpret_cast<const uint4*>(x + j0);
-        const uint4 uw = *reinterpret_cast<const uint4*>(w + j0);
-        const T* a = reinterpret_cast<const T*>(&ux);
-        const T* b = reinterpret_cast<const T*>(&uw);
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+        if (i < nc) {
+            const T* a = reinterpret_cast<const T*>(&ux[i]);
+            const T* b = reinterpret_cast<const T*>(&uw[i]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc = fma(to_d<T>(a[q]), to_d<T>(b[q]), acc);
+        }
+    for (int j0 = 8 * lane + 256 * MAXC; j0 < H; j0 += 256) {     // longer rows
+        const uint4 a4 = *reinterpret_cast<const uint4*>(x + j0);
+        const uint4 b4 = *reinterpret_cast<const uint4*>(w + j0);
+        const T* a = reinterpret_cast<const T*>(&a4);
+        const T* b = reinterpret_cast<const T*>(&b4);
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc = fma(to_d<T>(a[q]), to_d<T>(b[q]), acc);
     }
@@ -130,11 +148,13 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
     const int has = shared_id >= 0;
     const int C = E + has;                 // logit columns: experts, then the shared gate
     const int slots = k + has;
-    const int c = blockIdx.x;
-    const T* w = c < E ? gate + (size_t)c * H : sgate;
-    for (int r = warp; r < R; r += RW) {
-        const double acc = logit64<T>(x + (size_t)r * x_stride, w, H, lane);
-        if (lane == 0) logits[(size_t)r * C + c] = c < E ? round_bf16_d(acc) : (float)acc;
+    const int c = blockIdx.x * RW + warp;      // a warp a logit column, every row
+    if (c < C) {
+        const T* w = c < E ? gate + (size_t)c * H : sgate;
+        for (int r = 0; r < R; ++r) {
+            const double acc = logit64<T>(x + (size_t)r * x_stride, w, H, lane);
+            if (lane == 0) logits[(size_t)r * C + c] = c < E ? round_bf16_d(acc) : (float)acc;
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -282,12 +302,12 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
     const int C = E + has;
     int rc;
     if (x_dtype == ESP_DTYPE_BF16)
-        rc = launch(route_kernel<__nv_bfloat16>, dim3(C), dim3(RT), 0, stream, true,
+        rc = launch(route_kernel<__nv_bfloat16>, dim3((C + RW - 1) / RW), dim3(RT), 0, stream, true,
                     static_cast<const __nv_bfloat16*>(x), x_stride, R, H, static_cast<const __nv_bfloat16*>(gate), E,
                     static_cast<const __nv_bfloat16*>(sgate), k, shared_id, logits, counter, pick_out, wts_out, uids,
                     ucount, members, maxm, maxu);
     else
-        rc = launch(route_kernel<__half>, dim3(C), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
+        rc = launch(route_kernel<__half>, dim3((C + RW - 1) / RW), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
                     R, H, static_cast<const __half*>(gate), E, static_cast<const __half*>(sgate), k, shared_id, logits,
                     counter, pick_out, wts_out, uids, ucount, members, maxm, maxu);
     if (rc) return rc;
