@@ -138,16 +138,17 @@ __device__ __forceinline__ uint64_t global_ns() {
 constexpr uint64_t WAIT_NS = 200ull * 1000 * 1000;   // a wait gives up after 0.2 s of wall time, never hangs
 
 // Wait for the phase of `parity` to complete. Gives up after WAIT_NS (time, not polls: a suspended try_wait may sleep),
-// records ESP_ERR_TIMEOUT and returns false. Once any wait of this file's kernels has timed out, later waits that do
-// not complete at once fail at once too, so a broken pipeline ends in one WAIT_NS, not one a stage.
+// records ESP_ERR_TIMEOUT and returns false. Once any wait of this file's kernels has timed out, a later wait gives up
+// after 20 us instead, so a broken pipeline ends in about one WAIT_NS, not one a stage.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
     const uint64_t t0 = global_ns();
     while (true) {
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > WAIT_NS) break;
+        const uint64_t dt = global_ns() - t0;
+        if (dt > WAIT_NS) break;
+        if (dt > 20000 && *reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
     }
     report(ESP_ERR_TIMEOUT);
     return false;

@@ -291,24 +291,35 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             }
             __syncwarp();
             const int n = nmats * nkt;
-            int mi = 0, kt = kt0;
+            // per-lane copy plan of the item. With two matrices their units alternate (gate kt0, up kt0, gate kt0 + 1,
+            // ...), so consumer group 0 decodes matrix 0 only and group 1 matrix 1. Weight chunks q = lane + 32 i of a
+            // unit (a unit = the 8 tiles of block b at one k-tile, contiguous); member-slice chunks q0 = lane,
+            // q1 = lane + 32 (member q >> 1, half q & 1). Each matrix's pointers advance one k-tile after its unit.
+            const size_t kstA = (size_t)(p.N / 16) * (8 * K0), kstB = (size_t)(p.N / 16) * (8 * K1);
+            const uint32_t* wA = T0 + ((size_t)kt0 * (p.N / 16) + (size_t)b * 8) * (8 * K0) + 4 * lane;
+            const uint32_t* wB = T1 + ((size_t)kt0 * (p.N / 16) + (size_t)b * 8) * (8 * K1) + 4 * lane;
+            const bool x0v = lane < 2 * nm, x1v = lane + 32 < 2 * nm;
+            const size_t xo0 = x0v ? (size_t)d.rows[lane >> 1] * p.K + kt0 * 16 + (lane & 1) * 8 : 0;
+            const size_t xo1 = x1v ? (size_t)d.rows[(lane + 32) >> 1] * p.K + kt0 * 16 + (lane & 1) * 8 : 0;
+            const __half *xA = X0 + xo0, *xA1 = X0 + xo1, *xB = X1 + xo0, *xB1 = X1 + xo1;
+            const int xd0 = GUPS * UNIT_WMAX + ((lane & 1) * MP + (lane >> 1)) * 4;
+            const int xd1 = xd0 + 16 * 4;                      // member + 16
             for (int i0 = 0; i0 < n; i0 += GUPS) {
                 if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
                 uint32_t* st = smem + (size_t)slot * STAGE_W;
                 const int m0 = min(GUPS, n - i0);
                 for (int j = 0; j < m0; ++j) {
-                    const int TW = 8 * (mi ? K1 : K0);
-                    const uint32_t* src = (mi ? T1 : T0) + ((size_t)kt * (p.N / 16) + (size_t)b * 8) * TW;
-                    for (int q = lane; q < 2 * TW; q += 32) cp_async16(st + j * UNIT_WMAX + q * 4, src + q * 4);
-                    const __half* X = mi ? X1 : X0;
-                    for (int q = lane; q < 2 * nm; q += 32) {
-                        const int m = q >> 1, h = q & 1;
-                        cp_async16(st + GUPS * UNIT_WMAX + j * SLICE_W + (h * MP + m) * 4,
-                                   X + (size_t)d.rows[m] * p.K + kt * 16 + h * 8);
-                    }
-                    if (++kt == kt0 + nkt) {
-                        kt = kt0;
-                        mi = 1;
+                    const bool mB = nmats == 2 && (j & 1);
+                    const uint32_t* wp = mB ? wB : wA;
+                    const int wq = 64 * (mB ? K1 : K0);        // words a unit
+                    uint32_t* du = st + j * UNIT_WMAX;
+                    for (int q = 4 * lane; q < wq; q += 128) cp_async16(du + q, wp + (q - 4 * lane));
+                    if (x0v) cp_async16(st + j * SLICE_W + xd0, mB ? xB : xA);
+                    if (x1v) cp_async16(st + j * SLICE_W + xd1, mB ? xB1 : xA1);
+                    if (mB) {
+                        wB += kstB; xB += 16; xB1 += 16;
+                    } else {
+                        wA += kstA; xA += 16; xA1 += 16;
                     }
                 }
                 cp_async_arrive(&full[slot]);
@@ -329,30 +340,27 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     constexpr int CT = GWARPS * 32;
     int slot = 0, phase = 0, di = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
-        float acc[2][2][NTG][4];      // [matrix][even/odd unit][token group][4]
+        float acc[2][NTG][4];      // [even/odd unit of this group][token group][4]
 #pragma unroll
-        for (int m = 0; m < 2; ++m)
+        for (int e2 = 0; e2 < 2; ++e2)
 #pragma unroll
-            for (int e2 = 0; e2 < 2; ++e2)
-#pragma unroll
-                for (int q = 0; q < NTG; ++q) acc[m][e2][q][0] = acc[m][e2][q][1] = acc[m][e2][q][2] = acc[m][e2][q][3] = 0.f;
+            for (int q = 0; q < NTG; ++q) acc[e2][q][0] = acc[e2][q][1] = acc[e2][q][2] = acc[e2][q][3] = 0.f;
         const ItemDesc* d = &desc[di];
-        int nkt = 0, nmats = 0, ntg = 0, cb0 = 0, K0 = 0, cb1 = 0, K1 = 0;
+        int nkt = 0, nmats = 0, ntg = 0, mcb = 0, mK = 0;
         for (int i0 = 0;; i0 += GUPS) {
             mbar_wait(&full[slot], phase);
             if (i0 == 0) {   // the descriptor is published with the item's first stage
                 nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
-                cb0 = d->cb0; K0 = d->K0; cb1 = d->cb1; K1 = d->K1;
+                const bool mB = nmats == 2 && grp == 1;      // with two matrices, group = matrix
+                mcb = mB ? d->cb1 : d->cb0;
+                mK = mB ? d->K1 : d->K0;
             }
             const int n = nmats * nkt;
             const uint32_t* st = smem + (size_t)slot * STAGE_W;
-            const uint32_t* xs0 = st + GUPS * UNIT_WMAX;
             const int m0 = min(GUPS, n - i0);
-            const int split_at = min(m0, max(0, nkt - i0));     // units of matrix 0 in this stage
-            if (split_at > 0)
-                dispatch_units<NTG, KCAP>(cb0, K0, st, xs0, 0, split_at, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[0]);
-            if (m0 > split_at)
-                dispatch_units<NTG, KCAP>(cb1, K1, st, xs0, split_at, m0, UNIT_WMAX, SLICE_W, grp, wl, lane, ntg, acc[1]);
+            if (m0 > 0)
+                dispatch_units<NTG, KCAP>(mcb, mK, st, st + GUPS * UNIT_WMAX, 0, m0, UNIT_WMAX, SLICE_W, grp, wl, lane,
+                                          ntg, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             if (++slot == GSTAGES) {
@@ -362,27 +370,29 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             if (i0 + GUPS >= n) break;
         }
 
-        // ---- the item's sums: group 0 then group 1, even + odd units, into red[matrix][member][column] ----
+        // ---- the item's sums, even + odd units, into red[matrix][member][column]: with two matrices each group
+        //      writes its own; with one, group 0 writes and group 1 adds ----
         const int col = wl * 16 + g;
         for (int gi = 0; gi < 2; ++gi) {
-            if (gi == grp)
+            if (gi == grp || nmats == 2) {
+                const bool add = nmats == 1 && gi == 1;
+                float* base = red + (size_t)(nmats == 2 ? grp : 0) * MP * GRED + col;
 #pragma unroll
-                for (int m = 0; m < 2; ++m)
-#pragma unroll
-                    for (int q = 0; q < NTG; ++q) {
-                        if (m >= nmats) continue;
-                        const int r0 = 8 * q + 2 * t;
-                        float* rr = red + ((size_t)m * MP + r0) * GRED + col;
-                        const float v0 = acc[m][0][q][0] + acc[m][1][q][0], v1 = acc[m][0][q][1] + acc[m][1][q][1];
-                        const float v2 = acc[m][0][q][2] + acc[m][1][q][2], v3 = acc[m][0][q][3] + acc[m][1][q][3];
-                        if (gi == 0) {
-                            rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
-                        } else {
-                            rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
-                        }
+                for (int q = 0; q < NTG; ++q) {
+                    float* rr = base + (size_t)(8 * q + 2 * t) * GRED;
+                    const float v0 = acc[0][q][0] + acc[1][q][0], v1 = acc[0][q][1] + acc[1][q][1];
+                    const float v2 = acc[0][q][2] + acc[1][q][2], v3 = acc[0][q][3] + acc[1][q][3];
+                    if (!add) {
+                        rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
+                    } else {
+                        rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
                     }
+                }
+            }
             named_sync(1, CT);
+            if (nmats == 2) break;
         }
+        const int cb0 = d->cb0, cb1 = d->cb1;
         const int e = d->e, b = d->b, nm = d->nm;
         const int n0 = b * 128 + 4 * lane;
         int u, bb, z;
