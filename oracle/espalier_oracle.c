@@ -18,7 +18,8 @@
  *   down + combine ....... vllm_espalier/csrc/experts.cu:340-393
  *   grouping ............. vllm_espalier/csrc/experts.cu:23-76, route.cu:132-179
  *   routing .............. vllm_espalier/csrc/route.cu:49-128, with the logit reduction order of this project's
- *                          routing kernel (fp64, fixed lane order; see orc_router_logit) so ids are exact.
+ *                          routing kernel (fp64 sums of fp32 products, fixed lane order; see orc_router_logit)
+ *                          so ids are exact.
  *
  * Build: oracle/Makefile (gcc -O2 -fopenmp -shared).
  */
@@ -326,27 +327,29 @@ void orc_had(const uint16_t* x, int M, int K, const uint16_t* pre, const uint16_
 /* Routing                                                                                                        */
 /* ------------------------------------------------------------------------------------------------------------ */
 
-/* Router logit of one (row, column) in this project's order: 32 lanes, lane l sums (in fp64, fused multiply-add,
- * starting from 0) the products x[j] * w[j] for j = 8 l + 256 i + q, i ascending then q = 0..7 ascending; then the
- * 32 lane sums are combined by an xor tree over offsets 16, 8, 4, 2, 1 (value of lane l becomes s_l + s_{l^o}), and
- * lane 0's value is the logit. bf16 x bf16 products are exact, so only the additions round. */
+/* Router logit of one (row, column) in this project's order: 32 lanes; lane l keeps 8 partial sums s_q (fp64, from
+ * 0), adding to s_q the product x[j] * w[j] for j = 8 l + 256 i + q, i ascending; each product is formed in fp32 and
+ * widened to fp64 (a bf16 x bf16 or fp16 x fp16 product has at most 22 significant bits, so it is exact unless it is
+ * below 2^-126 or overflows fp32: only bf16 pairs far outside any model's range). The lane's value is
+ * ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)); the 32 lane values are combined by an xor tree over offsets
+ * 16, 8, 4, 2, 1 (value of lane l becomes v_l + v_{l^o}), and lane 0's value is the logit. */
 double orc_router_logit(const uint16_t* x, const uint16_t* w, int H) {
-    double s[32];
+    double v[32];
     for (int l = 0; l < 32; ++l) {
-        double acc = 0.0;
+        double s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int j0 = 8 * l; j0 < H; j0 += 256)
             for (int q = 0; q < 8; ++q) {
-                const int j = j0 + q;
-                acc = fma((double)orc_bf2f(x[j]), (double)orc_bf2f(w[j]), acc);
+                const float pr = orc_bf2f(x[j0 + q]) * orc_bf2f(w[j0 + q]);
+                s[q] = s[q] + (double)pr;
             }
-        s[l] = acc;
+        v[l] = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
     }
     for (int o = 16; o > 0; o >>= 1) {
         double t[32];
-        for (int l = 0; l < 32; ++l) t[l] = s[l] + s[l ^ o];
-        memcpy(s, t, sizeof(t));
+        for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
+        memcpy(v, t, sizeof(t));
     }
-    return s[0];
+    return v[0];
 }
 
 /* Grouping (experts.cu:23-76): distinct experts < E in id order, members row * 32 + slot in (row, slot) order,

@@ -6,15 +6,17 @@
 // the shared slot (id shared_id) gets sigmoid(x . sgate) in fp32; grouping lists the distinct experts in id order and,
 // per expert, its members row * 32 + slot in (row, slot) order, padded with -1.
 //
-// Exactness (BASELINE: expert ids bit-exact against exact routing): each logit is an order-fixed fp64 reduction of the
-// exact bf16 x bf16 products (lane l of a warp sums j = 8 l + 256 i + q, i ascending then q = 0..7, by fused
-// multiply-add from 0; the 32 lane sums meet in an xor tree over offsets 16..1), rounded once to bf16. The CPU oracle
-// (oracle/espalier_oracle.c orc_router_logit) is the same order, so ids match bit for bit, and the fp64 sum is exact
-// to far below bf16 resolution, so they equal the correctly rounded logits' choice. Top-k compares bf16 logit values
-// (exp is monotone), so the choice does not depend on the exponential's last bit.
+// Exactness (expert ids bit-exact against exact routing): each logit is an order-fixed fp64 reduction of the exact
+// bf16 x bf16 products (lane l of a warp keeps 8 partial sums s_q of the products j = 8 l + 256 i + q, i ascending;
+// the lane's value is ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)); the 32 lane values meet in an xor tree
+// over offsets 16..1), rounded once to bf16. The CPU oracle (oracle/espalier_oracle.c orc_router_logit) is the same
+// order, so ids match bit for bit, and the fp64 sum is exact to far below bf16 resolution, so they equal the
+// correctly rounded logits' choice. Top-k compares bf16 logit values (exp is monotone), so the choice does not depend
+// on the exponential's last bit.
 //
-// B200 layout: a warp a logit column (E experts + the shared gate), all of its loads in flight at once; the last CTA to arrive
-// (acq_rel counter) does the per-row selection (a warp a row) and the grouping, then resets the counter.
+// B200 layout: a warp a (logit column, 2 rows) over a 2-D grid (E experts + the shared gate by row pairs), all of its
+// loads in flight at once; the last CTA to arrive (acq_rel counter) does the per-row selection (a warp a row) and the
+// grouping, then resets the counter.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -33,46 +35,82 @@ constexpr int MAX_K = 16;
 constexpr int MAX_E = 512;              // experts (incl. the shared slot) the grouping handles
 constexpr int MAX_PICKS = 32 * 33;      // rows x slots of one window
 
-template <typename T> __device__ __forceinline__ double to_d(T v);
-template <> __device__ __forceinline__ double to_d<__nv_bfloat16>(__nv_bfloat16 v) { return (double)__bfloat162float(v); }
-template <> __device__ __forceinline__ double to_d<__half>(__half v) { return (double)__half2float(v); }
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 
-// fp64 logit of one row against one weight row, in the documented order; every lane returns the full sum. All of the
-// lane's loads are issued before the first fused multiply-add (H <= 2048: at most 8 chunks of 8 a lane).
+// fp64 logits of up to RB rows against one weight row, each in the documented order: lane l keeps 8 partial sums s_q,
+// adding the product x[j] * w[j] (formed in fp32, exact for bf16 / fp16 pairs unless below 2^-126, then widened) for
+// j = 8 l + 256 i + q, i ascending; the lane's value is ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)); the lanes
+// meet in an xor tree over offsets 16..1. Every lane returns the full sums. The 8 * RB chains are independent; all of
+// the lane's loads are issued before the first addition (H <= 2048: at most 8 chunks of 8 a lane).
+constexpr int RB = 2;   // rows a warp
+
 template <typename T>
-__device__ __forceinline__ double logit64(const T* __restrict__ x, const T* __restrict__ w, int H, int lane) {
+__device__ __forceinline__ void add_chunk(const uint4& a4, const float (&wf)[8], double (&s)[8]) {
+    const T* a = reinterpret_cast<const T*>(&a4);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s[q] = __dadd_rn(s[q], (double)__fmul_rn(to_f<T>(a[q]), wf[q]));
+}
+
+template <typename T>
+__device__ __forceinline__ void logits64(const T* __restrict__ x, long long x_stride, int nr, const T* __restrict__ w,
+                                         int H, int lane, double (&acc)[RB]) {
     constexpr int MAXC = 8;
-    uint4 ux[MAXC], uw[MAXC];
+    uint4 uw[MAXC], ux[RB][MAXC];
     const int nc = (H - 8 * lane + 255) / 256;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i)
         if (i < nc) {
-            ux[i] = *reinterpret_cast<const uint4*>(x + 8 * lane + 256 * i);
             uw[i] = *reinterpret_cast<const uint4*>(w + 8 * lane + 256 * i);
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+                if (r < nr) ux[r][i] = *reinterpret_cast<const uint4*>(x + (size_t)r * x_stride + 8 * lane + 256 * i);
         }
-    double acc = 0.0;
+    double s[RB][8];
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) s[r][q] = 0.0;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i)
         if (i < nc) {
-            const T* a = reinterpret_cast<const T*>(&ux[i]);
-            const T* b = reinterpret_cast<const T*>(&uw[i]);
+            float wf[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc = fma(to_d<T>(a[q]), to_d<T>(b[q]), acc);
+            for (int q = 0; q < 8; ++q) wf[q] = to_f<T>(reinterpret_cast<const T*>(&uw[i])[q]);
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+                if (r < nr) add_chunk<T>(ux[r][i], wf, s[r]);
         }
     for (int j0 = 8 * lane + 256 * MAXC; j0 < H; j0 += 256) {     // longer rows
-        const uint4 a4 = *reinterpret_cast<const uint4*>(x + j0);
         const uint4 b4 = *reinterpret_cast<const uint4*>(w + j0);
-        const T* a = reinterpret_cast<const T*>(&a4);
-        const T* b = reinterpret_cast<const T*>(&b4);
+        float wf[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc = fma(to_d<T>(a[q]), to_d<T>(b[q]), acc);
+        for (int q = 0; q < 8; ++q) wf[q] = to_f<T>(reinterpret_cast<const T*>(&b4)[q]);
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+            if (r < nr) add_chunk<T>(*reinterpret_cast<const uint4*>(x + (size_t)r * x_stride + j0), wf, s[r]);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    return acc;
+    for (int r = 0; r < RB; ++r) {
+        acc[r] = __dadd_rn(__dadd_rn(__dadd_rn(s[r][0], s[r][1]), __dadd_rn(s[r][2], s[r][3])),
+                           __dadd_rn(__dadd_rn(s[r][4], s[r][5]), __dadd_rn(s[r][6], s[r][7])));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[r] = __dadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+    }
+}
+
+// Top-k keys: a bf16 logit and its id as one 32-bit key whose unsigned order is (value, then lower id) order: the
+// value's bits mapped to an order-preserving 16-bit code (-0 taken as +0, as a float compare does), then 0xffff - id.
+__device__ __forceinline__ uint32_t topk_key(float v, int e) {
+    const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+    const uint32_t k16 = (b & 0x80000000u) ? (~b >> 16) : ((b >> 16) | 0x8000u);
+    return (k16 << 16) | (0xffffu - (uint32_t)e);
+}
+__device__ __forceinline__ float topk_value(uint32_t key) {
+    const uint32_t k16 = key >> 16;
+    const uint32_t b16 = (k16 & 0x8000u) ? (k16 ^ 0x8000u) : (~k16 & 0xffffu);
+    return __uint_as_float(b16 << 16);
 }
 
 __device__ __forceinline__ float round_bf16_d(double v) {
@@ -132,6 +170,69 @@ __device__ void group_block(const int* sh_pick, int n, int slots, int n_ids, int
     }
 }
 
+// The grouping of route's own picks, whose ids are distinct within a row (top-k of distinct ids plus the shared id)
+// and whose rows number at most 32: a row bitmask an id (shared-memory atomicOr), the distinct ids in id order by a
+// block scan, then an id's members row by row (ascending) with the slot found in that row. Same output as group_block.
+__device__ void group_distinct(const int* sh_pick, int R, int slots, int n_ids, int* __restrict__ uids,
+                               int* __restrict__ ucount, int* __restrict__ members, int maxm, int maxu) {
+    __shared__ unsigned sh_mask[MAX_E];
+    __shared__ int warp_tot[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int e = threadIdx.x; e < n_ids; e += blockDim.x) sh_mask[e] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * slots; i += blockDim.x) {
+        const int e = sh_pick[i];
+        if (e >= 0 && e < n_ids) atomicOr(&sh_mask[e], 1u << (i / slots));
+    }
+    __syncthreads();
+    const int per = (n_ids + blockDim.x - 1) / blockDim.x;    // ids a thread (<= 2 with 256 threads, 512 ids)
+    unsigned mk[2] = {0u, 0u};
+    int used = 0;
+    for (int q = 0; q < per && q < 2; ++q) {
+        const int e = threadIdx.x * per + q;
+        mk[q] = e < n_ids ? sh_mask[e] : 0u;
+        used += mk[q] != 0u;
+    }
+    int inc = used;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = lane < nw ? warp_tot[lane] : 0;
+        int s = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x2 = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += x2;
+        }
+        if (lane < nw) warp_tot[lane] = s - v;
+        if (lane == 31) ucount[0] = s;
+    }
+    __syncthreads();
+    int place = warp_tot[warp] + inc - used;
+    for (int q = 0; q < per && q < 2; ++q) {
+        unsigned m = mk[q];
+        if (m == 0u) continue;
+        const int e = threadIdx.x * per + q;
+        if (place < maxu) {
+            uids[place] = e;
+            int j = 0;
+            for (; m != 0u && j < maxm; m &= m - 1u) {
+                const int r = __ffs(m) - 1;
+                int sl = 0;
+                while (sh_pick[r * slots + sl] != e) ++sl;     // present: the row's bit is set
+                members[place * maxm + j++] = r * 32 + sl;
+            }
+            for (; j < maxm; ++j) members[place * maxm + j] = -1;
+        }
+        ++place;
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long long x_stride, int R, int H,
                                                    const T* __restrict__ gate, int E, const T* __restrict__ sgate,
@@ -148,75 +249,69 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
     const int has = shared_id >= 0;
     const int C = E + has;                 // logit columns: experts, then the shared gate
     const int slots = k + has;
-    const int c = blockIdx.x * RW + warp;      // a warp a logit column, every row
+    const int c = blockIdx.x * RW + warp;      // a warp a (logit column, RB rows)
+    const int r0 = blockIdx.y * RB;
     if (c < C) {
         const T* w = c < E ? gate + (size_t)c * H : sgate;
-        for (int r = 0; r < R; ++r) {
-            const double acc = logit64<T>(x + (size_t)r * x_stride, w, H, lane);
-            if (lane == 0) logits[(size_t)r * C + c] = c < E ? round_bf16_d(acc) : (float)acc;
-        }
+        const int nr = min(RB, R - r0);
+        double acc[RB];
+        logits64<T>(x + (size_t)r0 * x_stride, x_stride, nr, w, H, lane, acc);
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+            if (r < nr && lane == 0) logits[(size_t)(r0 + r) * C + c] = c < E ? round_bf16_d(acc[r]) : (float)acc[r];
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         fence_acq_rel_gpu();
-        last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+        last = atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
         fence_acq_rel_gpu();
     }
     __syncthreads();
     if (!last) return;
 
-    // per row (a warp a row): top-k of the bf16 logits, lowest id on ties; weights over the selected k
+    // per row (a warp a row): top-k of the bf16 logits, lowest id on ties (a warp max over the keys a pick, the
+    // winner's key cleared); lane t keeps pick t; weights exp(l_t - l_0) / sum, summed in pick order
     for (int r = warp; r < R; r += RW) {
         const float* lr = logits + (size_t)r * C;
-        float v[MAX_E / 32];
+        uint32_t key[MAX_E / 32];
 #pragma unroll
         for (int q = 0; q < MAX_E / 32; ++q) {
             const int e = lane + 32 * q;
-            v[q] = e < E ? __ldcg(lr + e) : -INFINITY;
+            key[q] = e < E ? topk_key(__ldcg(lr + e), e) : 0u;
         }
-        int ids[MAX_K];
-        float lv[MAX_K];
+        int my_id = 0;
+        float my_v = 0.f;
         for (int t = 0; t < k; ++t) {
-            float bv = -INFINITY;
-            int be = 1 << 30;
+            uint32_t m = key[0];
 #pragma unroll
-            for (int q = 0; q < MAX_E / 32; ++q) {
-                const int e = lane + 32 * q;
-                if (e < E && (v[q] > bv || (v[q] == bv && e < be))) { bv = v[q]; be = e; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-                if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-            }
-            ids[t] = be;
-            lv[t] = bv;
+            for (int q = 1; q < MAX_E / 32; ++q) m = max(m, key[q]);
+            const uint32_t best = __reduce_max_sync(0xffffffffu, m);
 #pragma unroll
             for (int q = 0; q < MAX_E / 32; ++q)
-                if (lane + 32 * q == be) v[q] = -INFINITY;
+                if (key[q] == best) key[q] = 0u;
+            if (lane == t) {
+                my_id = (int)(0xffffu - (best & 0xffffu));
+                my_v = topk_value(best);
+            }
         }
-        if (lane == 0) {
-            float p[MAX_K], sum = 0.f;
-            for (int t = 0; t < k; ++t) {
-                p[t] = expf(lv[t] - lv[0]);
-                sum += p[t];
-            }
-            for (int t = 0; t < k; ++t) {
-                pick_out[r * slots + t] = ids[t];
-                wts_out[r * slots + t] = p[t] / sum;
-            }
-            if (has) {
-                pick_out[r * slots + k] = shared_id;
-                wts_out[r * slots + k] = 1.f / (1.f + expf(-__ldcg(lr + E)));
-            }
+        const float v0 = __shfl_sync(0xffffffffu, my_v, 0);
+        const float pt = expf(my_v - v0);
+        float sum = 0.f;
+        for (int t = 0; t < k; ++t) sum += __shfl_sync(0xffffffffu, pt, t);
+        if (lane < k) {
+            pick_out[r * slots + lane] = my_id;
+            wts_out[r * slots + lane] = pt / sum;
+        }
+        if (has && lane == 0) {
+            pick_out[r * slots + k] = shared_id;
+            wts_out[r * slots + k] = 1.f / (1.f + expf(-__ldcg(lr + E)));
         }
     }
     __syncthreads();
     const int n = R * slots;
     for (int i = threadIdx.x; i < n; i += RT) sh_pick[i] = pick_out[i];
     __syncthreads();
-    group_block(sh_pick, n, slots, E + has, uids, ucount, members, maxm, maxu);
+    group_distinct(sh_pick, R, slots, E + has, uids, ucount, members, maxm, maxu);
     if (threadIdx.x == 0) *counter = 0;
 }
 
@@ -294,7 +389,7 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
     ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "route_group: x must be bf16 or fp16");
     ESP_REQUIRE(E >= 1 && E + has <= MAX_E && k >= 1 && k <= MAX_K && k <= E && H % 256 == 0 && H > 0, ESP_ERR_INVALID,
                 "route_group: shape limits");
-    ESP_REQUIRE(R >= 1 && R * (k + has) <= MAX_PICKS && k + has <= 32, ESP_ERR_INVALID, "route_group: window too large");
+    ESP_REQUIRE(R >= 1 && R <= 32 && k + has <= 32, ESP_ERR_INVALID, "route_group: at most 32 rows and 32 slots");
     ESP_REQUIRE(!has || sgate, ESP_ERR_INVALID, "the shared gate weight is needed with a shared slot");
     ESP_REQUIRE(aligned(x, 16) && aligned(gate, 16) && (!has || aligned(sgate, 16)) && x_stride % 8 == 0,
                 ESP_ERR_INVALID, "route_group: rows must be 16-byte aligned");
@@ -302,12 +397,12 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
     const int C = E + has;
     int rc;
     if (x_dtype == ESP_DTYPE_BF16)
-        rc = launch(route_kernel<__nv_bfloat16>, dim3((C + RW - 1) / RW), dim3(RT), 0, stream, true,
+        rc = launch(route_kernel<__nv_bfloat16>, dim3((C + RW - 1) / RW, (R + RB - 1) / RB), dim3(RT), 0, stream, true,
                     static_cast<const __nv_bfloat16*>(x), x_stride, R, H, static_cast<const __nv_bfloat16*>(gate), E,
                     static_cast<const __nv_bfloat16*>(sgate), k, shared_id, logits, counter, pick_out, wts_out, uids,
                     ucount, members, maxm, maxu);
     else
-        rc = launch(route_kernel<__half>, dim3((C + RW - 1) / RW), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
+        rc = launch(route_kernel<__half>, dim3((C + RW - 1) / RW, (R + RB - 1) / RB), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
                     R, H, static_cast<const __half*>(gate), E, static_cast<const __half*>(sgate), k, shared_id, logits,
                     counter, pick_out, wts_out, uids, ucount, members, maxm, maxu);
     if (rc) return rc;
