@@ -37,7 +37,16 @@ namespace {
 constexpr int GWARPS = 16;                         // consumer warps (two groups of 8)
 constexpr int GTHREADS = (GWARPS + 1) * 32;
 constexpr int GUPS = 8;                            // units a stage
-constexpr int GSTAGES = 4;
+// Stage ring depth of an instance: as many stages as fit next to the reduction buffers in about 200 KB of dynamic
+// shared memory (the static tables take the rest of the 227 KB), at most 12. Deep rings keep 20-50 KB of weights in
+// flight an SM, enough to cover HBM latency with the small units of 1-3 bit experts.
+__host__ __device__ constexpr int stage_words(int ntg, int kcap) { return 8 * (8 * 8 * kcap + 8 * ntg * 8); }
+__host__ __device__ constexpr int red_bytes(int ntg) { return 2 * 8 * ntg * 132 * 4; }
+__host__ __device__ constexpr int gstages(int ntg, int kcap) {
+    return (200 * 1024 - red_bytes(ntg)) / (stage_words(ntg, kcap) * 4) < 12
+               ? (200 * 1024 - red_bytes(ntg)) / (stage_words(ntg, kcap) * 4)
+               : 12;
+}
 constexpr int GRED = 132;                          // fp32 row stride of the reduction buffers
 
 enum Mode : int { MODE_Z = 0, MODE_GATEUP = 1, MODE_DOWN = 2 };
@@ -198,7 +207,9 @@ struct ItemDesc {
     int cb0, K0, cb1, K1;
     int rows[32];          // slot index p of each member
 };
-constexpr int NDESC = 8;   // descriptor ring (an item spans at least one stage; the ring is 4 stages deep)
+// descriptor ring: the producer runs at most GSTAGES stages (so items) ahead; a slot is rewritten only after the
+// consumers finished the item NDESC back, which needs NDESC >= GSTAGES + 2
+constexpr int NDESC = 16;
 constexpr int MAX_PEND = 1024;     // deferred arrivals a CTA (items a CTA x members an item)
 
 // Work item `it` of MODE: (expert position u, block b, z); z = split (fused modes) or mat * S + split (MODE_Z).
@@ -211,6 +222,8 @@ __device__ __forceinline__ void item_coords(const GroupedParams& p, int it, int 
 
 template <int NTG, int KCAP>
 __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_constant__ GroupedParams p) {
+    constexpr int GSTAGES = gstages(NTG, KCAP);
+    static_assert(GSTAGES >= 2 && GSTAGES + 2 <= NDESC, "stage ring / descriptor ring");
     constexpr int MP = 8 * NTG;
     constexpr int UNIT_WMAX = 8 * 8 * KCAP;            // words of a unit at the widest width served
     constexpr int SLICE_W = MP * 8;                    // words of a k-tile's member slice: [2][MP][8 halves]
@@ -645,8 +658,8 @@ __global__ void combine_kernel(const float* __restrict__ y, const float* __restr
 }
 
 size_t grouped_smem(int ntg, int kcap) {
-    const int mp = 8 * ntg;
-    return (size_t)GSTAGES * GUPS * (8 * 8 * kcap + mp * 8) * 4 + (size_t)2 * mp * GRED * 4 + 2 * GSTAGES * 8;
+    const int st = gstages(ntg, kcap);
+    return (size_t)st * stage_words(ntg, kcap) * 4 + (size_t)red_bytes(ntg) + 2 * st * 8;
 }
 
 template <int NTG, int KCAP>
