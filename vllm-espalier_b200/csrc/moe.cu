@@ -11,8 +11,9 @@
 //
 // B200 pipeline (4 launches after this file's kernels: route, rot_in, gate+up, down):
 //   * grouped_kernel decodes, per distinct expert u (uids / members from the routing), the 8 tiles of a 128-column
-//     block b at each k-tile of its k-slice, from a shared-memory stage ring filled by a producer warp with 16-byte
-//     cp.async (the expert's tiles and its members' rotated activation slices), 16 consumer warps, one tile a warp,
+//     block b at each k-tile of its k-slice, from a shared-memory stage ring filled by two producer warps with
+//     16-byte cp.async (the expert's tiles and its members' rotated activation slices; gate and up units alternate, a
+//     producer and a consumer group to each matrix), 16 consumer warps, one tile a warp,
 //     mma.sync m16n8k16 with the weights as A (16 output columns) and up to 32 member rows as N. The codebook and width
 //     are dispatched per expert matrix at run time (experts mix E2M1 1/2-bit and int5 3-bit; the shared one is int6).
 //   * MODE_Z writes fp32 partial sums Z[mat][split][p][n] (the reference's `grouped` contract).
@@ -35,7 +36,8 @@ namespace esp {
 namespace {
 
 constexpr int GWARPS = 16;                         // consumer warps (two groups of 8)
-constexpr int GTHREADS = (GWARPS + 1) * 32;
+constexpr int GPROD = 2;                           // producer warps (units of even / odd position in a stage)
+constexpr int GTHREADS = (GWARPS + GPROD) * 32;
 constexpr int GUPS = 8;                            // units a stage
 // Stage ring depth of an instance: as many stages as fit next to the reduction buffers in about 200 KB of dynamic
 // shared memory (the static tables take the rest of the 227 KB), at most 12. Deep rings keep 20-50 KB of weights in
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     const int n_items = p.ucount[0] * NB * NZ;         // grid: one CTA an SM, items round robin
     if (threadIdx.x == 0) {
         for (int i = 0; i < GSTAGES; ++i) {
-            mbar_init(&full[i], 33);                   // 32 copy arrivals + the producer's release of descriptors
+            mbar_init(&full[i], 32 * GPROD + 1);       // the producers' copy arrivals + the release of descriptors
             mbar_init(&empty[i], GWARPS);
         }
         s_npend = 0;
@@ -274,12 +276,16 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     }
     if ((int)blockIdx.x >= n_items) return;
 
-    if (warp == GWARPS) {   // ---------------- producer ----------------
+    if (warp >= GWARPS) {   // ---------------- producers ----------------
+        // Producer pw copies the units of position j = pw (mod 2) of every stage: with two matrices (gate, up units
+        // alternate) that is matrix pw; with one, every other k-tile. Both compute each item's descriptor from global
+        // memory; producer 0 writes it to shared memory and releases it with the item's stages.
+        const int pw = warp - GWARPS;
+        const uint32_t sbase = smem_addr(smem);
         int slot = 0, phase = 0, nstage = 0, di = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
             int u, b, z;
             item_coords(p, it, NB, NZ, u, b, z);
-            ItemDesc& d = desc[di];
             const int e = p.uids[u];
             const int split = p.mode == MODE_Z ? z % p.S : z;
             const int mat0 = p.mode == MODE_Z ? z / p.S : 0;
@@ -288,55 +294,52 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             const int code = lane < p.maxm ? p.members[u * p.maxm + lane] : -1;
             const int row = code >= 0 ? (code >> 5) * p.slots + (code & 31) : -1;
             const int nm = __popc(__ballot_sync(0xffffffffu, row >= 0));
-            const int cb0 = p.cb[mat0][e], cb1 = p.cb[mmB][e];
-            const int K0 = p.k2[mat0][e] / 2, K1 = p.k2[mmB][e] / 2;
-            const uint32_t* T0 = reinterpret_cast<const uint32_t*>(p.tp[mat0][e]);
-            const uint32_t* T1 = reinterpret_cast<const uint32_t*>(p.tp[mmB][e]);
-            const __half* X0 = p.X[mat0];
-            const __half* X1 = p.X[mmB];
             const int kt0 = split * KT / p.S, nkt = (split + 1) * KT / p.S - kt0;
-            // the descriptor slot was last read by the consumers' epilogue of item (this - NDESC), which ended before
-            // they released the stage this item's first units need
-            d.rows[lane] = row;
-            if (lane == 0) {
-                d.e = e; d.b = b; d.split = split; d.mat0 = mat0; d.nmats = nmats; d.kt0 = kt0; d.nkt = nkt;
-                d.nm = nm; d.cb0 = cb0; d.K0 = K0; d.cb1 = cb1; d.K1 = K1;
+            if (pw == 0) {
+                // the descriptor slot was last read by the consumers' epilogue of item (this - NDESC), which ended
+                // before they released the stage this item's first units need
+                ItemDesc& d = desc[di];
+                d.rows[lane] = row;
+                if (lane == 0) {
+                    d.e = e; d.b = b; d.split = split; d.mat0 = mat0; d.nmats = nmats; d.kt0 = kt0; d.nkt = nkt;
+                    d.nm = nm; d.cb0 = p.cb[mat0][e]; d.K0 = p.k2[mat0][e] / 2; d.cb1 = p.cb[mmB][e];
+                    d.K1 = p.k2[mmB][e] / 2;
+                }
+                __syncwarp();
             }
-            __syncwarp();
             const int n = nmats * nkt;
-            // per-lane copy plan of the item. With two matrices their units alternate (gate kt0, up kt0, gate kt0 + 1,
-            // ...), so consumer group 0 decodes matrix 0 only and group 1 matrix 1. Weight chunks q = lane + 32 i of a
-            // unit (a unit = the 8 tiles of block b at one k-tile, contiguous); member-slice chunks q0 = lane,
-            // q1 = lane + 32 (member q >> 1, half q & 1). Each matrix's pointers advance one k-tile after its unit.
-            const size_t kstA = (size_t)(p.N / 16) * (8 * K0), kstB = (size_t)(p.N / 16) * (8 * K1);
-            const uint32_t* wA = T0 + ((size_t)kt0 * (p.N / 16) + (size_t)b * 8) * (8 * K0) + 4 * lane;
-            const uint32_t* wB = T1 + ((size_t)kt0 * (p.N / 16) + (size_t)b * 8) * (8 * K1) + 4 * lane;
+            // this producer's stream: matrix m, first k-tile ktA, kstep k-tiles a unit
+            const int m = nmats == 2 ? mat0 + pw : mat0;
+            const int kstep = nmats == 2 ? 1 : 2;
+            const int ktA = kt0 + (nmats == 2 ? 0 : pw);
+            const int Km = p.k2[m][e] / 2;
+            const size_t kst = (size_t)(p.N / 16) * (8 * Km) * kstep;   // words between this stream's units
+            const uint32_t* wp =
+                reinterpret_cast<const uint32_t*>(p.tp[m][e]) + ((size_t)ktA * (p.N / 16) + (size_t)b * 8) * (8 * Km) + 4 * lane;
+            const int wq = 16 * Km;                                          // 16-byte chunks a unit
+            // member-slice chunks q0 = lane, q1 = lane + 32 (member q >> 1, half q & 1)
+            const int r0 = __shfl_sync(0xffffffffu, row, (lane >> 1) & 31);
+            const int r1 = __shfl_sync(0xffffffffu, row, ((lane + 32) >> 1) & 31);
             const bool x0v = lane < 2 * nm, x1v = lane + 32 < 2 * nm;
-            const size_t xo0 = x0v ? (size_t)d.rows[lane >> 1] * p.K + kt0 * 16 + (lane & 1) * 8 : 0;
-            const size_t xo1 = x1v ? (size_t)d.rows[(lane + 32) >> 1] * p.K + kt0 * 16 + (lane & 1) * 8 : 0;
-            const __half *xA = X0 + xo0, *xA1 = X0 + xo1, *xB = X1 + xo0, *xB1 = X1 + xo1;
-            const int xd0 = GUPS * UNIT_WMAX + ((lane & 1) * MP + (lane >> 1)) * 4;
-            const int xd1 = xd0 + 16 * 4;                      // member + 16
+            const __half* xp0 = p.X[m] + (x0v ? (size_t)r0 * p.K + ktA * 16 + (lane & 1) * 8 : 0);
+            const __half* xp1 = p.X[m] + (x1v ? (size_t)r1 * p.K + ktA * 16 + (lane & 1) * 8 : 0);
+            const uint32_t xd0 = 4 * (GUPS * UNIT_WMAX + ((lane & 1) * MP + (lane >> 1)) * 4);
+            const uint32_t xd1 = xd0 + 16 * 16;                               // member + 16
             for (int i0 = 0; i0 < n; i0 += GUPS) {
                 if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
-                uint32_t* st = smem + (size_t)slot * STAGE_W;
+                const uint32_t sb = sbase + (uint32_t)slot * (STAGE_W * 4);
                 const int m0 = min(GUPS, n - i0);
-                for (int j = 0; j < m0; ++j) {
-                    const bool mB = nmats == 2 && (j & 1);
-                    const uint32_t* wp = mB ? wB : wA;
-                    const int wq = 64 * (mB ? K1 : K0);        // words a unit
-                    uint32_t* du = st + j * UNIT_WMAX;
-                    for (int q = 4 * lane; q < wq; q += 128) cp_async16(du + q, wp + (q - 4 * lane));
-                    if (x0v) cp_async16(st + j * SLICE_W + xd0, mB ? xB : xA);
-                    if (x1v) cp_async16(st + j * SLICE_W + xd1, mB ? xB1 : xA1);
-                    if (mB) {
-                        wB += kstB; xB += 16; xB1 += 16;
-                    } else {
-                        wA += kstA; xA += 16; xA1 += 16;
-                    }
+                for (int j = pw; j < m0; j += 2) {
+                    const uint32_t du = sb + j * (UNIT_WMAX * 4) + 16 * lane;
+                    for (int q = 0; q < wq - lane; q += 32) cp_async16_sa(du + 16 * q, wp + 4 * q);
+                    if (x0v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd0, xp0);
+                    if (x1v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd1, xp1);
+                    wp += kst;
+                    xp0 += 16 * kstep;
+                    xp1 += 16 * kstep;
                 }
                 cp_async_arrive(&full[slot]);
-                if (lane == 0) mbar_arrive(&full[slot]);      // releases this item's descriptor with the stage
+                if (pw == 0 && lane == 0) mbar_arrive(&full[slot]);    // releases this item's descriptor with the stage
                 ++nstage;
                 if (++slot == GSTAGES) {
                     slot = 0;
