@@ -107,6 +107,122 @@ size_t esp_dense_z_bytes(int m);
 int esp_dense_noalloc(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats,
                       int n_mats, int k2, int cb, void* y, int y_dtype, long long y_stride, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * MoE routing and grouping. A window is R <= 32 rows with `slots` picks each (k routed, plus the shared expert as
+ * the last slot when shared_id >= 0). Grouping: uids[0..ucount) = the distinct expert ids in ascending order, and per
+ * distinct expert u its members[u * maxm + j] = row * 32 + slot in (row, slot) order, padded with -1.
+ * --------------------------------------------------------------------------------------------------------------- */
+
+/*
+ * Router GEMV (x . gate[e] for E experts, plus x . sgate for the shared slot), bf16 rounding of the expert logits,
+ * top-k with the lowest id on ties, weights exp(l - l_max) / sum over the k picks, sigmoid of the shared logit, and
+ * the grouping, in one launch. Logits are order-fixed fp64 sums of exact products (the CPU oracle reproduces them
+ * bit for bit), so the ids equal exact routing's. logits: fp32 [R][E + 1]; counter: int32, zero before the first
+ * call and left zero; pick_out / wts_out: [R][k (+1)]. maxm >= R. x / gate / sgate: bf16 or fp16 (x_dtype).
+ * Replaces ext().route_group(x, gate, sgate, k, shared_id, logits, counter, pick, wts, uids, ucount, members)
+ *                                              (vllm_espalier/csrc/experts.cpp:214-224, route.cu:35-181).
+ */
+int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                    const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                    int* uids, int* ucount, int* members, int maxm, int maxu, void* stream);
+
+/*
+ * Grouping of a given pick table pick[R][slots] (ids outside [0, E) are skipped).
+ * Replaces ext().group(pick, uids, ucount, members, R, slots, E)  (vllm_espalier/csrc/experts.cpp:79-90,
+ *                                                                    experts.cu:23-76).
+ */
+int esp_group(const int* pick, int R, int slots, int E, int* uids, int* ucount, int* members, int maxm, int maxu,
+              void* stream);
+
+/*
+ * vLLM's routed picks [R][slots_in] plus the shared expert as an extra last slot with weight sigmoid(x . gate_w)
+ * (fp32), written to pick_out / wts_out [R][slots_in + 1], then the grouping.
+ * Replaces ext().group_shared(pick_in, wts_in, x, x_stride, gate_w, shared_id, pick_out, wts_out, uids, ucount,
+ *                             members, R, slots_in, E)  (vllm_espalier/csrc/experts.cpp:154-173, experts.cu:247-330).
+ */
+int esp_group_shared(const int* pick_in, const float* wts_in, const void* x, int x_dtype, long long x_stride, int H,
+                     const void* gate_w, int shared_id, int* pick_out, float* wts_out, int* uids, int* ucount,
+                     int* members, int R, int slots_in, int E, int maxm, int maxu, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Grouped experts. Expert tables are device arrays indexed by expert id: trellis pointers (int64 [E]), half-bits k2
+ * (int32 [E]) and kernel codebook ids (int32 [E]); k2_host / cb_host are host copies ([mats][E]) so that the set of
+ * (codebook, width) instances is checked on the host. Slot p = row * slots + j; P = rows * slots.
+ * --------------------------------------------------------------------------------------------------------------- */
+
+/*
+ * out0 / out1 fp16 [P][K] = fp16(H(x[row] * suh0/1[pick[p]]) / sqrt(128)) for every slot with a valid expert.
+ * Replaces ext().rot_in(x, x_stride, pick, suh0, suh1, out0, out1, rows, K, slots, E)
+ *                                              (vllm_espalier/csrc/experts.cpp:92-104, experts.cu:97-115).
+ */
+int esp_rot_in(const void* x, int x_dtype, long long x_stride, const int* pick, const uint16_t* suh0,
+               const uint16_t* suh1, uint16_t* out0, uint16_t* out1, int rows, int K, int slots, int E, void* stream);
+
+/*
+ * Z fp32 [mats][SK][P][N] = the grouped decode GEMV's partial sums of X0/X1 (fp16 [P][K]) against each member's
+ * expert matrices, split in SK equal k-slices (the reference's `grouped` contract, its tile parameters nt / warps /
+ * pf / lo / hi having no counterpart here).
+ * Replaces ext().grouped(X0, X1, TP0, TP1, B0, B1, C0, C1, uids, ucount, members, Z, mats, K, N, P, SK, slots, nt,
+ *                        warps, pf, lo, hi)    (vllm_espalier/csrc/experts.cpp:44-66, experts_grouped.cuh).
+ */
+int esp_grouped(const uint16_t* X0, const uint16_t* X1, const int64_t* TP0, const int64_t* TP1, const int* B0,
+                const int* B1, const int* C0, const int* C1, const int* k2_host, const int* cb_host, int E,
+                const int* uids, const int* ucount, const int* members, int maxu, int maxm, float* Z, int mats, int K,
+                int N, int P, int SK, int slots, void* stream);
+
+/*
+ * Fused gate + up + SwiGLU: xd fp16 [P][I] for every slot with a valid expert, equal to grouped(mats = 2) followed
+ * by gateup_epilogue(act_mode 1, no limit). S > 1 splits D in S k-slices whose fp32 partials go to Z
+ * ([2][S][P][I]) and are added in slice order by the last of the S to finish; counters (int32, maxu * I / 128,
+ * zero and left zero) count the arrivals. No single counterpart: replaces the reference's grouped + gateup_epilogue
+ * pair of launches (vllm_espalier/experts.py routed2).
+ */
+int esp_moe_gateup(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u,
+                   const int* k2_g, const int* k2_u, const int* cb_g, const int* cb_u, const int* k2_host,
+                   const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u, const uint16_t* suh_d,
+                   const int* uids, const int* ucount, const int* members, int maxu, int maxm, int slots, int P, int D,
+                   int I, int S, float* Z, int* counters, uint16_t* xd, void* stream);
+
+/*
+ * Fused down + combine: y fp32 [P][D] per slot, out [rows][D] = the routed slots' sum of w * y in slot order (fp32
+ * fused multiply-adds from 0) and out_shared [rows][D] = w * y of the shared slot (slot n_routed, when
+ * n_routed < slots), both in out_dtype; rows without a valid slot get zeros. counters: int32, rows * D / 128, zero and
+ * left zero. Equals grouped(mats = 1) + down_combine2. No single counterpart: replaces the reference's grouped +
+ * down_combine2 pair of launches (vllm_espalier/experts.py routed2).
+ */
+int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const int* cb_d, const int* k2_host,
+                 const int* cb_host, int E, const uint16_t* svh_d, const int* uids, const int* ucount,
+                 const int* members, int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed,
+                 int rows, int I, int D, float* y, int* counters, void* out, void* out_shared, int out_dtype,
+                 void* stream);
+
+/*
+ * xd fp16 [P][N] from the gate / up partial sums Z [2][SK][P][N] (act_mode 0: bf16-rounded SwiGLU with `limit`,
+ * 1: fp32 SwiGLU).
+ * Replaces ext().gateup_epilogue(Z, pick, svh_g, svh_u, suh_d, xd, rows, P, N, SK, slots, E, limit, act_mode)
+ *                                              (vllm_espalier/csrc/experts.cpp:106-118, experts.cu:120-162).
+ */
+int esp_gateup_epilogue(const float* Z, const int* pick, const uint16_t* svh_g, const uint16_t* svh_u,
+                        const uint16_t* suh_d, uint16_t* xd, int rows, int P, int N, int SK, int slots, int E,
+                        float limit, int act_mode, void* stream);
+
+/*
+ * y fp32 [P][D] = H(sum of the SK down partials) / sqrt(128) * svh_d; with combine != 0 also out [rows][D] (sum of
+ * the first n_routed slots' w * y in slot order) and, when out_shared != NULL, out_shared = w * y of slot n_routed.
+ * Replaces ext().down_epilogue (combine = 0), ext().down_combine (fp32 out, n_routed = slots) and
+ * ext().down_combine2 (out_dtype out + out_shared)  (vllm_espalier/csrc/experts.cpp:120-129, 139-152, 175-191,
+ *                                                     experts.cu:340-393).
+ */
+int esp_down_combine(const float* Z, const int* pick, const uint16_t* svh_d, float* y, const float* wts, void* out,
+                     void* out_shared, int out_dtype, int rows, int P, int D, int SK, int slots, int E, int n_routed,
+                     int combine, void* stream);
+
+/*
+ * out fp32 [rows][D] = sum over slots of w * y (fused multiply-adds from 0, slot order).
+ * Replaces ext().combine(y, wts, out, rows, D, slots)  (vllm_espalier/csrc/experts.cpp:131-137, experts.cu:187-195).
+ */
+int esp_combine(const float* y, const float* wts, float* out, int rows, int D, int slots, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,14 +24,17 @@ namespace esp {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// mcg pair (experts_grouped.cuh:64-79): x = s * 0xCBAC1FED; x = (x & 0x8FFF8FFF) ^ 0x3B603B60; v = fp16 lo + fp16 hi
+// mcg pair (experts_grouped.cuh:64-79): x = s * 0xCBAC1FED; x = (x & 0x8FFF8FFF) ^ 0x3B603B60; v = fp16 lo + fp16 hi.
+// Each sum is one fp16 add of the word's two halves broadcast (v in both halves), and one permute packs v0, v1: a
+// permute fewer than gathering the low and the high halves first, on the ALU pipe that bounds the decode.
 __device__ __forceinline__ uint32_t mcg2(uint32_t s0, uint32_t s1) {
     uint32_t x0 = s0 * 0xCBAC1FEDu, x1 = s1 * 0xCBAC1FEDu;
     x0 = (x0 & 0x8FFF8FFFu) ^ 0x3B603B60u;
     x1 = (x1 & 0x8FFF8FFFu) ^ 0x3B603B60u;
-    const uint32_t lo = __byte_perm(x0, x1, 0x5410);
-    const uint32_t hi = __byte_perm(x0, x1, 0x7632);
-    return h2u(__hadd2(u2h(lo), u2h(hi)));
+    const __half2 h0 = u2h(x0), h1 = u2h(x1);
+    const __half2 v0 = __hadd2(__low2half2(h0), __high2half2(h0));
+    const __half2 v1 = __hadd2(__low2half2(h1), __high2half2(h1));
+    return h2u(__lows2half2(v0, v1));
 }
 
 // E2M1 in units of C = 0.75. The reference thresholds |v| at C * {.25, .75, 1.25, 1.75, 2.5, 3.5, 5} with strict '>'
