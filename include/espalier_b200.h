@@ -98,7 +98,7 @@ size_t esp_dense_z_bytes(int m);
  * esp_dense without any scratch argument and without allocating: for callers that cannot allocate device memory when
  * they run a layer (a serving engine whose KV cache already holds nearly all of HBM, a host bound only through this
  * C ABI with no allocator, a path that must not take cudaMalloc's implicit synchronisation). The scratch lives in one
- * fixed 3.6 MiB array of device memory that every GPU loading the library holds until the process exits.
+ * fixed 6.0 MiB array of device memory that every GPU loading the library holds until the process exits.
  * Limits: k <= 4096, sum(n) <= 1,048,576 output columns, m <= 32, a GPU with at most 160 SMs; larger calls return
  * ESP_ERR_INVALID. The first call on a device looks up the array's address (make it before any stream capture).
  * All calls share the array: calls that overlap on the GPU (other streams, other threads) race and must not be made.

@@ -167,6 +167,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // writes the barrier ordered before it, so the whole CTA's stores are published without a fence in every thread.
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Split-K / last-arriver arrival: one atomic add with release and acquire semantics at GPU scope, returning the old
+// value. Executed by one thread after a CTA barrier it publishes the whole CTA's earlier writes (release is cumulative
+// over what the barrier ordered before it) and, for the last arriver, makes the other arrivals' writes visible; one L2
+// round trip instead of fence + atomic + fence.
+__device__ __forceinline__ int arrive_acq_rel(int* counter) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+    return old;
+}
+
 // 16-byte asynchronous copy global -> shared (L2 only), and the arrive-on of an mbarrier when all of this thread's
 // earlier copies have landed (the arrival counts against the barrier's expected count).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

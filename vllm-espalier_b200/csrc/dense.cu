@@ -9,17 +9,20 @@
 //   * rot_kernel writes fp16 H(x * suh_s) / sqrt(128) for every matrix once, in a tile-major layout
 //     [s][k-tile][k-half][row][8] whose per-k-tile slice is one contiguous bulk copy (and bank-conflict free as an MMA
 //     B fragment).
-//   * dense_kernel: one CTA per SM (sized so that a second CTA, the next layer's, fits beside it and its programmatic
-//     dependent launch can prefetch that layer's weights while this one finishes). The layer is a list of units
-//     (128-column block, 16-row k-tile) in block-major order, split into equal contiguous ranges, one per CTA
-//     (stream-K), so every SM decodes the same number of weights. A producer warp streams each unit's 8 tiles (8K words
-//     each) and its activation slice into a ring of shared-memory stages with 16-byte cp.async from all 32 lanes,
-//     completing on mbarriers (a bulk copy a unit measured ~40 ns of TMA issue each, too slow for 1 KB units); 8 consumer
-//     warps decode tile w of every unit straight into the A fragment of mma.sync m16n8k16
-//     (M = 16 output columns, N = 8 tokens), i.e. each weight is decoded once whatever the number of rows.
-//   * A block whose k range is split across CTAs is finished by the last CTA to arrive (atomic counter), which adds
-//     the partial sums in CTA order; a block owned by one CTA is finished in place. Finishing = FWHT-128 of the sums,
-//     * step, * H/sqrt(128) * svh, in the reference's order, then the store in y's dtype.
+//   * dense_kernel: one CTA per SM. The layer is a list of units (128-column block, 16-row k-tile) in block-major
+//     order, split into G contiguous ranges, one per CTA: with fewer blocks than SMs, S = SMs / blocks equal k-slices
+//     of every block (G = blocks * S, one segment a CTA); otherwise G = SMs equal ranges over whole blocks. Two
+//     producer warps (the even and the odd units of each stage; one warp sharing a scheduler with four busy consumer
+//     warps could not keep the ring filled) stream each unit's 8 tiles (8K words each) and its activation slice into a
+//     ring of shared-memory stages with 16-byte cp.async from all 32 lanes, completing on mbarriers (a bulk copy a
+//     unit measured ~40 ns of TMA issue each, too slow for 1 KB units). 16 consumer warps in two groups (alternate
+//     units) decode tile w of every unit straight into the A fragment of mma.sync m16n8k16 (M = 16 output columns,
+//     N = 8 tokens), i.e. each weight is decoded once whatever the number of rows.
+//   * A block whose k range spans several CTAs' ranges is finished by the last of them to arrive (one acq_rel atomic
+//     a CTA and block), which adds their partial sums in CTA (= k) order; a block inside one CTA's range is finished in
+//     place. A CTA's range meets at most two partial blocks (its first and its last), stored in partial slots 2c and
+//     2c + 1. Finishing = FWHT-128 of the sums, * step, * H/sqrt(128) * svh, in the reference's order, then the store
+//     in y's dtype. The ranges depend on the shape and the SM count only.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -40,7 +43,11 @@ constexpr int MAX_SHARDS = 4;
 #endif
 constexpr int GROUPS = ESP_DENSE_GROUPS;       // consumer groups of 8 warps, taking alternate units of a stage
 constexpr int CWARPS = 8 * GROUPS;             // consumer warps: warp w decodes tile w % 8 of its group's units
-constexpr int THREADS = (CWARPS + 1) * 32;     // + one producer warp
+#ifndef ESP_DENSE_PRODUCERS
+#define ESP_DENSE_PRODUCERS 2
+#endif
+constexpr int PRODUCERS = ESP_DENSE_PRODUCERS;  // producer warps: unit j of a stage goes to producer j % PRODUCERS
+constexpr int THREADS = (CWARPS + PRODUCERS) * 32;
 constexpr int UPS = 8;                         // units per pipeline stage
 constexpr int STAGES = 6;                      // pipeline depth (stages of UPS units)
 constexpr int RED_STRIDE = 132;                // fp32 row stride of the reduction buffer (bank-conflict free)
@@ -69,10 +76,10 @@ struct DenseParams {
     void* y;
     int y_dtype;
     long long y_stride;
-    float* Z;                    // partial sums [2 * G][M][128]
+    float* Z;                    // partial sums [2 * G][M][128]: slot 2c = CTA c's first block, 2c + 1 its last
     int* counters;               // [blocks], zero on entry and on exit
-    int M, Mp, K, KT, U, G;      // rows, padded rows, inputs, k tiles, units, CTAs
-    int NB, S;                   // 128-column blocks; CTAs a block (0: whole blocks a CTA)
+    int M, Mp, K, KT, U, G;      // rows, padded rows, inputs, k tiles, units, CTAs (G <= U)
+    int NB;                      // 128-column blocks
     float scale;                 // codebook step of the kernel form
 };
 
@@ -114,13 +121,11 @@ __global__ void __launch_bounds__(128) rot_kernel(const __grid_constant__ RotPar
     *reinterpret_cast<uint2*>(p.xh + ((((size_t)s * p.KT + kt) * 2 + h) * p.Mp + m) * 8 + e) = u;
 }
 
-// First unit of CTA c. Split mode (fewer blocks than SMs): block c / S, k-tiles [i KT / S, (i + 1) KT / S) for
-// i = c % S, so no CTA straddles two blocks and each block has exactly S partial sums. Whole mode (S == 0): CTA c owns
-// blocks [c NB / G, (c + 1) NB / G) outright.
-__device__ __forceinline__ long long range_start(int c, const DenseParams& p) {
-    if (p.S == 0) return (long long)c * p.NB / p.G * p.KT;
-    return (long long)(c / p.S) * p.KT + (long long)(c % p.S) * p.KT / p.S;
-}
+// First unit of CTA c: the units (block-major, k-tile minor) split in G equal contiguous ranges (with G = blocks * S
+// these are the S k-slices of every block). U * G < 2^31 is checked on the host, so 32-bit arithmetic is exact.
+__device__ __forceinline__ int range_start(int c, const DenseParams& p) { return c * p.U / p.G; }
+// The CTA whose range holds unit u (the largest c with range_start(c) <= u).
+__device__ __forceinline__ int cta_of(int u, const DenseParams& p) { return ((u + 1) * p.G - 1) / p.U; }
 
 __device__ __forceinline__ uint2 load_svh(const DShard& S, int bl, int lane) {
     return *reinterpret_cast<const uint2*>(S.svh + bl * 128 + 4 * lane);
@@ -144,16 +149,6 @@ __device__ __forceinline__ int shard_of(int bg, const DenseParams& p) {
     for (int i = 1; i < MAX_SHARDS; ++i)
         if (i < p.n && bg >= p.s[i].nb0) s = i;
     return s;
-}
-
-// Source addresses of unit u (block bg, k-tile kt): its 8 tiles (contiguous) and its activation slice.
-template <int TW, int SLICE_H>
-__device__ __forceinline__ void unit_src(long long u, const DenseParams& p, const uint32_t*& w, const __half*& x) {
-    const int bg = (int)(u / p.KT), kt = (int)(u - (long long)bg * p.KT);
-    const int s = shard_of(bg, p);
-    const DShard& S = p.s[s];
-    w = S.T + ((size_t)kt * S.nb * 8 + (size_t)(bg - S.nb0) * 8) * TW;
-    x = p.xh + ((size_t)s * p.KT + kt) * SLICE_H;
 }
 
 // fp16 H(x[row] * suh) / sqrt(128) of 128-input chunks, stored as MMA B-fragment slices (k-tile, k-half, row, 8): the
@@ -212,14 +207,14 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
-    const long long u0 = range_start(c, p), u1 = range_start(c + 1, p);
-    const int n = (int)(u1 - u0);
+    const int u0 = range_start(c, p), u1 = range_start(c + 1, p);
+    const int n = u1 - u0;
     const int nst = (n + UPS - 1) / UPS;
-    const int bg0 = (int)(u0 / p.KT), kt0 = (int)(u0 - (long long)bg0 * p.KT);
+    const int bg0 = u0 / p.KT, kt0 = u0 - bg0 * p.KT;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&full[i], 32);       // one arrival a producer lane, when its copies of the stage have landed
+            mbar_init(&full[i], 32 * PRODUCERS);   // one arrival a producer lane, when its copies have landed
             mbar_init(&empty[i], CWARPS);
         }
         fence_mbar_init();
@@ -227,64 +222,75 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
     __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == CWARPS) {   // -------- producer warp: 16-byte async copies, all lanes, arrival on the stage's barrier --------
-        // unit j of a stage: its UNIT_W words in 16-byte pieces spread over the 32 lanes (and its activation slice)
-        int ubg = bg0, ukt = kt0, us = shard_of(bg0, p);
-        auto src_w = [&]() -> const uint32_t* {
-            const DShard& S = p.s[us];
-            return S.T + ((size_t)ukt * S.nb * 8 + (size_t)(ubg - S.nb0) * 8) * TW;
-        };
-        auto src_x = [&]() -> const __half* { return p.xh + ((size_t)us * p.KT + ukt) * (size_t)(2 * MP * 8); };
-        auto step = [&]() {
-            if (++ukt == p.KT) {
-                ukt = 0;
-                ++ubg;
-                if (us + 1 < p.n && ubg >= p.s[us + 1].nb0) ++us;
+    if (warp >= CWARPS) {   // -------- producer warps: 16-byte async copies, all lanes, arrival on the stage's barrier --------
+        // producer pw copies units j = pw, pw + PRODUCERS, ... of each stage (the CTA's units u0 + pw + PRODUCERS i):
+        // their UNIT_W words in 16-byte pieces spread over the 32 lanes (and their activation slices)
+        const int pw = warp - CWARPS;
+        const uint32_t sbase = smem_addr(smem);
+        struct Cur { int bg, kt, s; };
+        auto start = [&]() -> Cur {
+            Cur q{bg0, kt0 + pw, shard_of(bg0, p)};
+            if (q.kt >= p.KT) {
+                q.kt -= p.KT;
+                ++q.bg;
+                if (q.s + 1 < p.n && q.bg >= p.s[q.s + 1].nb0) ++q.s;
             }
+            return q;
+        };
+        auto step2 = [&](Cur& q) {   // PRODUCERS units on
+            q.kt += PRODUCERS;
+            if (q.kt >= p.KT) {
+                q.kt -= p.KT;
+                ++q.bg;
+                if (q.s + 1 < p.n && q.bg >= p.s[q.s + 1].nb0) ++q.s;
+            }
+        };
+        auto src_w = [&](const Cur& q) -> const uint32_t* {
+            const DShard& S = p.s[q.s];
+            return S.T + ((size_t)q.kt * S.nb * 8 + (size_t)(q.bg - S.nb0) * 8) * TW;
+        };
+        auto src_x = [&](const Cur& q) -> const uint32_t* {
+            return reinterpret_cast<const uint32_t*>(p.xh + ((size_t)q.s * p.KT + q.kt) * (size_t)(2 * MP * 8));
         };
         constexpr int WP = UNIT_W / 4;                 // 16-byte pieces of a unit's tiles
         constexpr int XP = SLICE_W / 4;                // ... of its activation slice
-        auto fill = [&](int i, int slot, bool w, bool x) {
-            uint32_t* st = smem + (size_t)slot * STAGE_W;
+        auto fill = [&](int i, int slot, bool w, bool x, Cur& q) {
+            const uint32_t st = sbase + (uint32_t)slot * (STAGE_W * 4);
             const int m = min(UPS, n - i * UPS);
-            for (int j = 0; j < m; ++j, step()) {
+            for (int j = pw; j < m; j += PRODUCERS, step2(q)) {
                 if (w) {
-                    const uint32_t* src = src_w();
+                    const uint32_t* src = src_w(q);
 #pragma unroll
-                    for (int q = lane; q < WP; q += 32) cp_async16(st + j * UNIT_W + q * 4, src + q * 4);
+                    for (int k = lane; k < WP; k += 32) cp_async16_sa(st + (j * UNIT_W + k * 4) * 4, src + k * 4);
                 }
                 if (x) {
-                    const __half* src = src_x();
-                    for (int q = lane; q < XP; q += 32)
-                        cp_async16(st + UPS * UNIT_W + j * SLICE_W + q * 4, reinterpret_cast<const uint32_t*>(src) + q * 4);
+                    const uint32_t* src = src_x(q);
+                    for (int k = lane; k < XP; k += 32)
+                        cp_async16_sa(st + (UPS * UNIT_W + j * SLICE_W + k * 4) * 4, src + k * 4);
                 }
             }
-            cp_async_arrive(&full[slot]);
         };
+        Cur cur = start();
         const int pre = min(nst, STAGES);
         if constexpr (FUSED) {
-            for (int i = 0; i < pre; ++i) fill(i, i, true, false);
+            for (int i = 0; i < pre; ++i) {
+                fill(i, i, true, false, cur);
+                cp_async_arrive(&full[i]);
+            }
         } else {
             // weights do not depend on the previous kernel: fetch them first, then (after the wait) the activations
-            const int bgs = ubg, kts = ukt, ss = us;
-            for (int i = 0; i < pre; ++i) {
-                uint32_t* st = smem + (size_t)i * STAGE_W;
-                const int m = min(UPS, n - i * UPS);
-                for (int j = 0; j < m; ++j, step()) {
-                    const uint32_t* src = src_w();
-#pragma unroll
-                    for (int q = lane; q < WP; q += 32) cp_async16(st + j * UNIT_W + q * 4, src + q * 4);
-                }
-            }
-            const int bge = ubg, kte = ukt, se = us;
-            ubg = bgs; ukt = kts; us = ss;
+            Cur c0 = cur;
+            for (int i = 0; i < pre; ++i) fill(i, i, true, false, cur);
             pdl_wait();
-            for (int i = 0; i < pre; ++i) fill(i, i, false, true);
-            ubg = bge; ukt = kte; us = se;
+            for (int i = 0; i < pre; ++i) {
+                fill(i, i, false, true, c0);
+                cp_async_arrive(&full[i]);
+            }
         }
         for (int i = STAGES, slot = 0, phase = 0; i < nst; ++i) {
             if (!mbar_wait(&empty[slot], phase)) return;
-            fill(i, slot, true, !FUSED);
+            fill(i, slot, true, !FUSED, cur);
+            cp_async_arrive(&full[slot]);
             if (++slot == STAGES) {
                 slot = 0;
                 phase ^= 1;
@@ -404,7 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
                 finish_store(v, lane, S, bl, r, p, sv);
             }
         } else {                         // partial: store it; the arrival on the block's counter waits for the end
-            float* zs = p.Z + (size_t)c * p.M * 128;     // split mode: one partial a CTA
+            float* zs = p.Z + (size_t)(2 * c + (bg == bg0 ? 0 : 1)) * p.M * 128;   // first / last block's slot
             for (int r = warp; r < p.M; r += CWARPS)
                 *reinterpret_cast<float4*>(zs + r * 128 + 4 * lane) =
                     *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
@@ -423,9 +429,8 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
         named_sync(1, CT);                 // every partial of this CTA is stored
         if (threadIdx.x < npend) {
             const int b = pend_bg[threadIdx.x];
-            fence_acq_rel_gpu();           // publish them (cumulative over the barrier) before arriving
-            s_lastv[threadIdx.x] = atomicAdd(&p.counters[b], 1) == p.S - 1;
-            fence_acq_rel_gpu();           // and see the other arrivals' partials if last
+            const int nc = cta_of(b * p.KT + p.KT - 1, p) - cta_of(b * p.KT, p) + 1;
+            s_lastv[threadIdx.x] = arrive_acq_rel(&p.counters[b]) == nc - 1;   // publishes / sees the partials
         }
         named_sync(1, CT);
         for (int pi = 0; pi < npend; ++pi) {
@@ -434,16 +439,21 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
             const DShard& S = p.s[shard_of(b, p)];
             const int bl = b - S.nb0;
             const uint2 sv = load_svh(S, bl, lane);
-            const int c_lo = b * p.S, c_hi = c_lo + p.S - 1;   // the block's CTAs, added in k order
+            // the block's CTAs, added in k order; only the first can hold it as its last block (slot 2c + 1)
+            const int c_lo = cta_of(b * p.KT, p), c_hi = cta_of(b * p.KT + p.KT - 1, p);
+            const int lo_slot = 2 * c_lo + (range_start(c_lo, p) < b * p.KT ? 1 : 0);
             for (int r = warp; r < p.M; r += CWARPS) {
                 float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int c8 = c_lo; c8 <= c_hi; c8 += 8) {
                     float4 q[8];
 #pragma unroll
-                    for (int d = 0; d < 8; ++d)
-                        q[d] = c8 + d <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)(c8 + d) * p.M + r) * 128 +
-                                                                                      4 * lane))
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int d = 0; d < 8; ++d) {
+                        const int cc = c8 + d;
+                        const int slot = cc == c_lo ? lo_slot : 2 * cc;
+                        q[d] = cc <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)slot * p.M + r) * 128 +
+                                                                                   4 * lane))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
 #pragma unroll
                     for (int d = 0; d < 8; ++d)
                         if (c8 + d <= c_hi) {
@@ -553,7 +563,7 @@ size_t esp_dense_xh_bytes(int m, int k, int n_mats) {
     return (size_t)n_mats * mp * k * 2;
 }
 
-size_t esp_dense_z_bytes(int m) { return (size_t)device_sms() * CTAS_PER_SM * m * 128 * 4; }
+size_t esp_dense_z_bytes(int m) { return (size_t)2 * device_sms() * CTAS_PER_SM * m * 128 * 4; }
 
 int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
               int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
@@ -601,25 +611,24 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
     p.KT = k / 16;
     p.U = nbt * p.KT;
     p.NB = nbt;
+    // Fewer blocks than SMs: S CTAs a block, each an equal k-slice, so a CTA has one segment and a block S partials
+    // (stream-K ranges over all SMs balance the decode better but pay a mid-range segment switch and a second
+    // partial a CTA, which measured slower). Otherwise one range an SM over whole blocks, with at most a partial
+    // block at each end.
     {
         const int sms = device_sms() * CTAS_PER_SM;
-        if (nbt >= sms) {            // whole blocks a CTA: no partial sums
-            p.S = 0;
-            p.G = sms;
-        } else {                     // S CTAs a block, each an equal k-slice (at least one k-tile)
-            p.S = std::min(sms / nbt, p.KT);
-            p.G = nbt * p.S;
-        }
+        p.G = nbt >= sms ? sms : nbt * std::min(sms / nbt, p.KT);
     }
+    ESP_REQUIRE((long long)p.U * p.G < (1ll << 31), ESP_ERR_INVALID, "esp_dense: layer too large (%d units)", p.U);
     p.scale = cb_step(cb);
     p.Z = z;
-    const size_t zneed = p.S ? (size_t)p.G * m * 128 * 4 : 0;
+    const size_t zneed = (size_t)2 * p.G * m * 128 * 4;
     ESP_REQUIRE((zneed == 0 || z) && z_bytes >= zneed && aligned(z, 16), ESP_ERR_SCRATCH,
                 "esp_dense: Z scratch needs %zu bytes, got %zu", zneed, z_bytes);
 
     // the fused path rotates each segment's inputs inside the kernel; a segment spans at most the CTA's units or one
     // block's k-tiles, plus one chunk of misalignment
-    const long long per_cta = p.S ? (p.KT + p.S - 1) / p.S : (long long)((p.NB + p.G - 1) / p.G) * p.KT;
+    const long long per_cta = (p.U + p.G - 1) / p.G;
     const int max_kt = (int)std::min<long long>(p.KT, per_cta);
     const int chunks = std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
     // up to 8 rows the in-kernel rotation is cheaper than a rotation launch; above, its loads serialise per row
@@ -701,10 +710,10 @@ namespace {
 constexpr int NOALLOC_MAX_K = 4096;            // input features
 constexpr int NOALLOC_MAX_BLOCKS = 8192;       // 128-column blocks of all matrices of one call (1,048,576 columns)
 constexpr int NOALLOC_MAX_SMS = 160;
-constexpr size_t NOALLOC_Z = (size_t)NOALLOC_MAX_SMS * 32 * 128 * 4;   // partial sums: a CTA x 32 rows x 128 cols
+constexpr size_t NOALLOC_Z = (size_t)2 * NOALLOC_MAX_SMS * 32 * 128 * 4;   // partial sums: 2 a CTA x 32 rows x 128 cols
 constexpr size_t NOALLOC_XH = (size_t)MAX_SHARDS * 32 * NOALLOC_MAX_K * 2;
 constexpr size_t NOALLOC_CNT = (size_t)NOALLOC_MAX_BLOCKS * 4;
-static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_Z + NOALLOC_XH + NOALLOC_CNT];   // 3.6 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_Z + NOALLOC_XH + NOALLOC_CNT];   // 6.0 MiB
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[64] = {nullptr};

@@ -479,9 +479,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                 target += e2 >= 0 && e2 < p.E;
             }
         }
-        fence_acq_rel_gpu();
-        s_last[i] = atomicAdd(&p.counters[s_pend[i][0]], 1) == target - 1;
-        fence_acq_rel_gpu();
+        s_last[i] = arrive_acq_rel(&p.counters[s_pend[i][0]]) == target - 1;
     }
     named_sync(1, CT);
     for (int pi = 0; pi < np; ++pi) {

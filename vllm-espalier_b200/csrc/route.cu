@@ -262,9 +262,7 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        fence_acq_rel_gpu();
-        last = atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
-        fence_acq_rel_gpu();
+        last = arrive_acq_rel(counter) == (int)(gridDim.x * gridDim.y) - 1;
     }
     __syncthreads();
     if (!last) return;
