@@ -103,7 +103,9 @@ class Step:
         self.graph.replay() if self.graph is not None else self.eager()
 
     def launches(self) -> int:
-        return 4 * len(self.blocks)      # per block: (rotation + fused decode) for qkv and for o
+        # per block and matrix set (qkv, o): one decode launch with the input rotation fused up to 8 rows, a rotation
+        # launch plus the decode launch above
+        return (2 if self.R <= 8 else 4) * len(self.blocks)
 
 
 class Clocks:
@@ -144,6 +146,119 @@ class Clocks:
         busy = [v for v in sm if v > 0]
         return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": float(rows[0][2]),
                 "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# one MoE layer, hidden 2048, 256 routed experts (gate/up 2048 -> 512, down 512 -> 2048) of
+# 1/2/3 bits with probabilities 0.3/0.5/0.2 (1-2 bit E2M1, 3 bit int5), a 4-bit int6 shared expert of intermediate
+# 512, a bf16 2048 x 256 router with softmax top-8. A step runs `layers` such layers (8 by default: 1.5 GB of expert
+# weights, 12x the L2) on the same input rows, each as route (one launch) + routed2 (rot_in, gate/up, down).
+# ---------------------------------------------------------------------------------------------------------------
+MOE_D, MOE_I, MOE_E, MOE_K = 2048, 512, 256, 8
+
+
+def build_moe(layers: int, dev, seed: int = 1):
+    import math
+    import numpy as np
+    __graft_entry__.load_package()
+    from vllm_espalier_b200 import experts as G
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    rng = np.random.default_rng(seed)
+
+    def mat(kin, n, K, grid):
+        return Mat.__new__(Mat).__init_moe__(kin, n, K, grid, gen, dev)
+    out = []
+    for _ in range(layers):
+        ex = []
+        for _e in range(MOE_E):
+            bits = int(rng.choice([1, 2, 3], p=[0.3, 0.5, 0.2]))
+            K, grid = (bits, 1) if bits < 3 else (3, 3)          # esp grid codes: 1 = E2M1, 3 = int5
+            ex.append((mat(MOE_D, MOE_I, K, grid), mat(MOE_D, MOE_I, K, grid), mat(MOE_I, MOE_D, K, grid)))
+        sh = (mat(MOE_D, MOE_I, 4, 4), mat(MOE_D, MOE_I, 4, 4), mat(MOE_I, MOE_D, 4, 4))   # 4 = int6
+        gw = (torch.randn(MOE_D, device=dev, generator=gen) / math.sqrt(MOE_D)).to(torch.bfloat16)
+        gate = (torch.randn(MOE_E, MOE_D, device=dev, generator=gen) / math.sqrt(MOE_D)).to(torch.bfloat16)
+        out.append((G.prepare(ex, sh, gw), gate, ex, sh))
+    return G, out
+
+
+def _init_moe(self, kin, n, K, grid, gen, dev):
+    self.trellis = torch.randint(-32768, 32768, (kin // 16, n // 16, 16 * K), dtype=torch.int16, device=dev,
+                                 generator=gen)
+    self.suh = (torch.randint(0, 2, (kin,), device=dev, generator=gen) * 2 - 1).half()
+    self.svh = ((torch.randint(0, 2, (n,), device=dev, generator=gen) * 2 - 1).float() *
+                (0.5 + torch.rand(n, device=dev, generator=gen)) / 64).half()
+    self.K, self.cb, self.in_features, self.out_features = K, grid, kin, n
+    return self
+
+
+Mat.__init_moe__ = _init_moe
+
+
+def _mat_bytes(m) -> int:
+    return m.trellis.numel() * 2 + m.suh.numel() * 2 + m.svh.numel() * 2
+
+
+class MoEStep:
+    """One decode step through the MoE layers at batch R (static buffers, graph-capturable)."""
+
+    def __init__(self, G, layers, R, dev):
+        self.G, self.layers, self.R = G, layers, R
+        self.x = torch.randn(R, MOE_D, device=dev).to(torch.bfloat16)
+        self.s = G.scratch(layers[0][0], 32, MOE_K + 1, dev)
+        self.outs = [(torch.empty(R, MOE_D, dtype=torch.bfloat16, device=dev),
+                      torch.empty(R, MOE_D, dtype=torch.bfloat16, device=dev)) for _ in layers]
+        self.graph = None
+
+    def eager(self):
+        for (L, gate, _, _), (o, so) in zip(self.layers, self.outs):
+            self.G.route(self.x, gate, MOE_K, L, self.s)
+            self.G.routed2(self.x, None, None, L, self.s, out=o, out_shared=so, k=MOE_K)
+
+    def capture(self):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.eager()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.eager()
+
+    def __call__(self):
+        self.graph.replay() if self.graph is not None else self.eager()
+
+    def touched_bytes(self) -> int:
+        """Compressed bytes one step reads: each layer's router and the matrices of every expert it picked."""
+        total = 0
+        for L, gate, ex, sh in self.layers:
+            self.G.route(self.x, gate, MOE_K, L, self.s)
+            torch.cuda.synchronize()
+            n = int(self.s.count[0].item())
+            ids, _ = self.s.window(self.R)
+            for e in ids[:n].tolist():
+                mats = sh if e == L.shared_id else ex[e]
+                total += sum(_mat_bytes(m) for m in mats)
+            total += gate.numel() * 2 + L.gate_w.numel() * 2
+        return total
+
+
+def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float) -> dict:
+    G, model = build_moe(layers, dev)
+    res = {}
+    for R in (1, 8, 32):
+        st = MoEStep(G, model, R, dev)
+        st.eager()
+        st.capture()
+        ms = time_steps(st, steps, warmup, dist, dev)
+        nbytes = st.touched_bytes()
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[str(R)] = {"us_per_layer": ms * 1e3 / layers, "tok_s_layer_stack": R / (ms * 1e-3),
+                       "touched_mb_per_layer": nbytes / layers / 1e6, "weight_gbs": gbs, "hbm_frac": gbs / peak}
+        st.graph = None
+    return {"workload": f"BASELINE configs[2]: {layers} MoE layers a step (256 experts 1/2/3-bit E2M1/int5, int6 "
+                        f"shared, top-8 router), fused routing + 3 expert launches a layer, graph replay",
+            "layers": layers, "launches_per_layer": 4, "batches": res}
 
 
 def peaks() -> tuple[float, str]:
@@ -293,6 +408,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--moe-layers", type=int, default=8)
+    ap.add_argument("--no-moe", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     dist, rank, ws, local = init_dist()
@@ -362,6 +479,8 @@ def main():
     }
     if rank == 0 and ws == 1 and not a.no_cpu:
         line["cpu_baseline"] = cpu_baseline(blocks, 1, a.layers, a.cpu_seconds)
+    if not a.no_moe:
+        line["moe"] = moe_bench(dev, a.moe_layers, max(a.steps // 8, 10), a.warmup, dist, peak)
     for st in steps_main.values():
         st.graph = None
     if rank == 0:
