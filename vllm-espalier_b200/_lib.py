@@ -98,14 +98,31 @@ def _check(t: torch.Tensor, dtype: torch.dtype, name: str):
     _need(t.is_cuda and t.dtype == dtype and t.is_contiguous(), f"{name}: expected a contiguous CUDA tensor of the right dtype")
 
 
+_private_z: dict = {}
+
+
+def _z_for(Z: torch.Tensor, M: int, device) -> torch.Tensor:
+    """The caller's Z when it holds esp_dense_z_bytes(M), else a private per-device buffer grown to that size: callers
+    that size Z by the reference's own plan (SK * 32 * N floats, vllm_espalier/dense.py:80-84) can fall short of this
+    library's split for some shapes (few k-tiles). Only the Python shim allocates; the C ABI never does."""
+    need = int(lib().esp_dense_z_bytes(M))
+    if Z.numel() * 4 >= need:
+        return Z
+    z = _private_z.get(device)
+    if z is None or z.numel() * 4 < need:
+        z = torch.empty(need // 4, dtype=torch.float32, device=device)
+        _private_z[device] = z
+    return z
+
+
 class _Ext:
     """The reference extension's functions over the C ABI."""
 
     # ---- dense layer (experts.cpp:193-211) ----
     @staticmethod
     def dense(x, T, suh, svh, col0, y, xh, Z, counters, k2, cb, SK=1, W=4, PF=1, rot_smem=0):
-        """SK / W / PF / rot_smem are the reference's tile-plan hints; this library plans its own tiling (stream-K over
-        all SMs) from the shape alone, so they are accepted and ignored."""
+        """SK / W / PF / rot_smem are the reference's tile-plan hints; this library plans its own split (k-slices of
+        every 128-column block over all SMs) from the shape alone, so they are accepted and ignored."""
         _need(x.is_cuda and x.dim() == 2 and x.stride(1) == 1, "x: CUDA [M, K], unit column stride")
         _need(y.is_cuda and y.dim() == 2 and y.stride(1) == 1, "y: CUDA [M, N], unit column stride")
         _need(len(T) == len(suh) == len(svh) == len(col0), "one entry a matrix")
@@ -123,6 +140,7 @@ class _Ext:
         _check(Z, torch.float32, "Z")
         _check(counters, torch.int32, "counters")
         _need(xh.is_cuda and xh.is_contiguous(), "xh: contiguous CUDA scratch")
+        Z = _z_for(Z, M, x.device)
         check(lib().esp_dense(x.data_ptr(), DTYPE[x.dtype], x.stride(0), M, K, mats, len(T), int(k2), int(cb),
                               y.data_ptr(), DTYPE[y.dtype], y.stride(0), xh.data_ptr(), xh.numel() * xh.element_size(),
                               Z.data_ptr(), Z.numel() * 4, counters.data_ptr(), counters.numel(),
