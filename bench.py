@@ -157,28 +157,38 @@ class Clocks:
 MOE_D, MOE_I, MOE_E, MOE_K = 2048, 512, 256, 8
 
 
-def build_moe(layers: int, dev, seed: int = 1):
+def build_moe(layers: int, dev, seed: int = 1, rank: int = 0, world: int = 1):
+    """The layers on one rank: every expert when world == 1, else the rank's expert range (the widths are drawn for
+    all experts on every rank, so all ranks agree on them) as EPLayer shares; the router is replicated."""
     import math
     import numpy as np
     __graft_entry__.load_package()
+    from vllm_espalier_b200 import ep as EP
     from vllm_espalier_b200 import experts as G
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed)
     rng = np.random.default_rng(seed)
+    e0, e1 = EP.expert_range(rank, world, MOE_E)
 
     def mat(kin, n, K, grid):
         return Mat.__new__(Mat).__init_moe__(kin, n, K, grid, gen, dev)
     out = []
     for _ in range(layers):
         ex = []
-        for _e in range(MOE_E):
+        for e in range(MOE_E):
             bits = int(rng.choice([1, 2, 3], p=[0.3, 0.5, 0.2]))
             K, grid = (bits, 1) if bits < 3 else (3, 3)          # esp grid codes: 1 = E2M1, 3 = int5
-            ex.append((mat(MOE_D, MOE_I, K, grid), mat(MOE_D, MOE_I, K, grid), mat(MOE_I, MOE_D, K, grid)))
+            ex.append((mat(MOE_D, MOE_I, K, grid), mat(MOE_D, MOE_I, K, grid), mat(MOE_I, MOE_D, K, grid))
+                      if e0 <= e < e1 else None)
         sh = (mat(MOE_D, MOE_I, 4, 4), mat(MOE_D, MOE_I, 4, 4), mat(MOE_I, MOE_D, 4, 4))   # 4 = int6
-        gw = (torch.randn(MOE_D, device=dev, generator=gen) / math.sqrt(MOE_D)).to(torch.bfloat16)
-        gate = (torch.randn(MOE_E, MOE_D, device=dev, generator=gen) / math.sqrt(MOE_D)).to(torch.bfloat16)
-        out.append((G.prepare(ex, sh, gw), gate, ex, sh))
+        gw = torch.Generator(device=dev)
+        gw.manual_seed(seed * 1000 + len(out))                  # the replicated router: the same on every rank
+        gate_w = (torch.randn(MOE_D, device=dev, generator=gw) / math.sqrt(MOE_D)).to(torch.bfloat16)
+        gate = (torch.randn(MOE_E, MOE_D, device=dev, generator=gw) / math.sqrt(MOE_D)).to(torch.bfloat16)
+        if world == 1:
+            out.append((G.prepare(ex, sh, gate_w), gate, ex, sh))
+        else:
+            out.append((EP.EPLayer(ex[e0:e1], sh, gate_w, rank, world, MOE_E, rows=32, k=MOE_K), gate, ex, sh))
     return G, out
 
 
@@ -200,20 +210,24 @@ def _mat_bytes(m) -> int:
 
 
 class MoEStep:
-    """One decode step through the MoE layers at batch R (static buffers, graph-capturable)."""
+    """One decode step through the MoE layers at batch R (static buffers, graph-capturable); expert parallel over the
+    ranks when the layers are EPLayer shares."""
 
-    def __init__(self, G, layers, R, dev):
-        self.G, self.layers, self.R = G, layers, R
+    def __init__(self, G, layers, R, dev, world: int = 1):
+        self.G, self.layers, self.R, self.world = G, layers, R, world
         self.x = torch.randn(R, MOE_D, device=dev).to(torch.bfloat16)
-        self.s = G.scratch(layers[0][0], 32, MOE_K + 1, dev)
+        self.s = G.scratch(layers[0][0], 32, MOE_K + 1, dev) if world == 1 else None
         self.outs = [(torch.empty(R, MOE_D, dtype=torch.bfloat16, device=dev),
                       torch.empty(R, MOE_D, dtype=torch.bfloat16, device=dev)) for _ in layers]
         self.graph = None
 
     def eager(self):
         for (L, gate, _, _), (o, so) in zip(self.layers, self.outs):
-            self.G.route(self.x, gate, MOE_K, L, self.s)
-            self.G.routed2(self.x, None, None, L, self.s, out=o, out_shared=so, k=MOE_K)
+            if self.world == 1:
+                self.G.route(self.x, gate, MOE_K, L, self.s)
+                self.G.routed2(self.x, None, None, L, self.s, out=o, out_shared=so, k=MOE_K)
+            else:
+                L.forward(self.x, gate, out=o, out_shared=so)
 
     def capture(self):
         s = torch.cuda.Stream()
@@ -229,7 +243,10 @@ class MoEStep:
         self.graph.replay() if self.graph is not None else self.eager()
 
     def touched_bytes(self) -> int:
-        """Compressed bytes one step reads: each layer's router and the matrices of every expert it picked."""
+        """Compressed bytes one step reads: each layer's router and the matrices of every expert it picked (one GPU;
+        with expert parallelism the bytes are reported as null)."""
+        if self.world > 1:
+            return 0
         total = 0
         for L, gate, ex, sh in self.layers:
             self.G.route(self.x, gate, MOE_K, L, self.s)
@@ -243,22 +260,27 @@ class MoEStep:
         return total
 
 
-def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float) -> dict:
-    G, model = build_moe(layers, dev)
+def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float, rank: int = 0, world: int = 1) -> dict:
+    G, model = build_moe(layers, dev, rank=rank, world=world)
     res = {}
     for R in (1, 8, 32):
-        st = MoEStep(G, model, R, dev)
+        st = MoEStep(G, model, R, dev, world)
         st.eager()
         st.capture()
         ms = time_steps(st, steps, warmup, dist, dev)
         nbytes = st.touched_bytes()
-        gbs = nbytes / (ms * 1e-3) / 1e9
-        res[str(R)] = {"us_per_layer": ms * 1e3 / layers, "tok_s_layer_stack": R / (ms * 1e-3),
-                       "touched_mb_per_layer": nbytes / layers / 1e6, "weight_gbs": gbs, "hbm_frac": gbs / peak}
+        gbs = nbytes / (ms * 1e-3) / 1e9 if nbytes else None
+        res[str(R)] = {"us_per_layer": ms * 1e3 / layers, "tok_s_layer_stack": world * R / (ms * 1e-3),
+                       "touched_mb_per_layer": nbytes / layers / 1e6 if nbytes else None, "weight_gbs": gbs,
+                       "hbm_frac": gbs / peak if gbs else None}
         st.graph = None
+    how = ("fused routing + 3 expert launches a layer" if world == 1 else
+           f"expert parallel over {world} GPUs: local routing, NCCL all_to_all dispatch of rows and picks, local "
+           f"experts, all_to_all of per-slot rows back, slot-ordered combine")
     return {"workload": f"BASELINE configs[2]: {layers} MoE layers a step (256 experts 1/2/3-bit E2M1/int5, int6 "
-                        f"shared, top-8 router), fused routing + 3 expert launches a layer, graph replay",
-            "layers": layers, "launches_per_layer": 4, "batches": res}
+                        f"shared, top-8 router), {how.strip()}, graph replay",
+            "layers": layers, "world": world, "scaling": "weak (R rows a rank)" if world > 1 else None,
+            "launches_per_layer": 4 if world == 1 else None, "batches": res}
 
 
 def peaks() -> tuple[float, str]:
@@ -480,7 +502,7 @@ def main():
     if rank == 0 and ws == 1 and not a.no_cpu:
         line["cpu_baseline"] = cpu_baseline(blocks, 1, a.layers, a.cpu_seconds)
     if not a.no_moe:
-        line["moe"] = moe_bench(dev, a.moe_layers, max(a.steps // 8, 10), a.warmup, dist, peak)
+        line["moe"] = moe_bench(dev, a.moe_layers, max(a.steps // 8, 10), a.warmup, dist, peak, rank, ws)
     for st in steps_main.values():
         st.graph = None
     if rank == 0:

@@ -223,6 +223,17 @@ int esp_down_combine(const float* Z, const int* pick, const uint16_t* svh_d, flo
  */
 int esp_combine(const float* y, const float* wts, float* out, int rows, int D, int slots, void* stream);
 
+/*
+ * Expert-parallel combine on a token's home rank (world ranks; rank q owns routed experts [q E / world,
+ * (q + 1) E / world)): out [R][D] = sum over the routed slots j < n_routed, in slot order (fp32 fused multiply-adds
+ * from 0), of wts * y, y taken from recv_y fp32 [world][R][slots][D] at the rank owning the slot's expert;
+ * out_shared = wts * y of slot n_routed (the shared expert, computed on the home rank) when out_shared != NULL. Same
+ * arithmetic as esp_moe_down's combine, so outputs are bit-identical for every world size. No counterpart in the
+ * reference (it has no expert parallelism).
+ */
+int esp_ep_combine(const float* recv_y, const int* pick, const float* wts, void* out, void* out_shared, int out_dtype,
+                   int R, int D, int slots, int n_routed, int E_routed, int world, int rank, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

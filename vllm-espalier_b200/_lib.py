@@ -55,6 +55,7 @@ SIGNATURES = {
     "esp_gateup_epilogue": (I, [P, P, P, P, P, P, I, I, I, I, I, I, F, I, P]),
     "esp_down_combine": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, P]),
     "esp_combine": (I, [P, P, P, I, I, I, P]),
+    "esp_ep_combine": (I, [P, P, P, P, P, I, I, I, I, I, I, I, I, P]),
     "esp_dense_z_bytes": (S, [I]),
 }
 

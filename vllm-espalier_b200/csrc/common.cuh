@@ -154,15 +154,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
-// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar` (no multicast).
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
-}
-
 // Release/acquire fence at GPU scope. One thread executes it after a CTA barrier: the fence is cumulative over the
 // writes the barrier ordered before it, so the whole CTA's stores are published without a fence in every thread.
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }

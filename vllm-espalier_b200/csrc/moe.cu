@@ -658,6 +658,46 @@ __global__ void combine_kernel(const float* __restrict__ y, const float* __restr
     out[(size_t)r * D + d] = acc;
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// Expert-parallel combine on a token's home rank: out[r] = sum over the routed slots j < n_routed (slot order, fp32
+// fma from 0) of w * y, where y is the slot's row returned by the rank owning its expert (rank of expert e =
+// ((e + 1) world - 1) / E_routed, i.e. experts [rank E / world, (rank + 1) E / world)); out_shared[r] = w * y of the
+// shared slot (computed on the home rank). The same arithmetic as the single-GPU fused down combine, so the outputs
+// are bit-identical for every world size. recv_y: fp32 [world][R][slots][D]. Block (row, 128-column block), a warp.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(32) ep_combine_kernel(const float* __restrict__ recv_y, const int* __restrict__ pick,
+                                                        const float* __restrict__ wts, void* out, void* out_shared,
+                                                        int out_dtype, int R, int D, int slots, int n_routed,
+                                                        int E_routed, int world, int rank) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x, lane = threadIdx.x;
+    const int n0 = blockIdx.y * 128 + 4 * lane;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < n_routed; ++j) {
+        const int e = pick[r * slots + j];
+        if (e < 0 || e >= E_routed) continue;
+        const int owner = ((e + 1) * world - 1) / E_routed;
+        const float w = wts[r * slots + j];
+        const float4 y = *reinterpret_cast<const float4*>(recv_y + (((size_t)owner * R + r) * slots + j) * D + n0);
+        acc[0] = fmaf(w, y.x, acc[0]);
+        acc[1] = fmaf(w, y.y, acc[1]);
+        acc[2] = fmaf(w, y.z, acc[2]);
+        acc[3] = fmaf(w, y.w, acc[3]);
+    }
+    store4(out, out_dtype, (size_t)r * D + n0, acc);
+    if (out_shared && n_routed < slots) {
+        const int j = n_routed;
+        float sv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (pick[r * slots + j] >= 0) {
+            const float w = wts[r * slots + j];
+            const float4 y = *reinterpret_cast<const float4*>(recv_y + (((size_t)rank * R + r) * slots + j) * D + n0);
+            sv[0] = w * y.x; sv[1] = w * y.y; sv[2] = w * y.z; sv[3] = w * y.w;
+        }
+        store4(out_shared, out_dtype, (size_t)r * D + n0, sv);
+    }
+}
+
 size_t grouped_smem(int ntg, int kcap) {
     const int st = gstages(ntg, kcap);
     return (size_t)st * stage_words(ntg, kcap) * 4 + (size_t)red_bytes(ntg) + 2 * st * 8;
@@ -857,6 +897,19 @@ int esp_down_combine(const float* Z, const int* pick, const uint16_t* svh_d, flo
         rc = launch(down_combine_kernel<float>, grid, block, 0, stream, true, Z, pick, sv, y, wts,
                     static_cast<float*>(out), static_cast<float*>(out_shared), P, D, SK, E, slots, n_routed, combine);
     if (rc) return rc;
+    return ok();
+}
+
+int esp_ep_combine(const float* recv_y, const int* pick, const float* wts, void* out, void* out_shared, int out_dtype,
+                   int R, int D, int slots, int n_routed, int E_routed, int world, int rank, void* stream) {
+    ESP_REQUIRE(recv_y && pick && wts && out, ESP_ERR_INVALID, "ep_combine: null pointer");
+    ESP_REQUIRE(D % 128 == 0 && slots >= 1 && slots <= 32 && n_routed <= slots && E_routed >= 1 && world >= 1 &&
+                    rank >= 0 && rank < world && out_dtype >= 0 && out_dtype <= 2,
+                ESP_ERR_INVALID, "ep_combine: limits");
+    if (R == 0) return ok();
+    if (int rc = launch(ep_combine_kernel, dim3((unsigned)R, (unsigned)(D / 128)), dim3(32), 0, stream, true, recv_y, pick,
+                        wts, out, out_shared, out_dtype, R, D, slots, n_routed, E_routed, world, rank))
+        return rc;
     return ok();
 }
 

@@ -33,7 +33,7 @@ constexpr int RT = 256;                 // threads a CTA
 constexpr int RW = RT / 32;
 constexpr int MAX_K = 16;
 constexpr int MAX_E = 512;              // experts (incl. the shared slot) the grouping handles
-constexpr int MAX_PICKS = 32 * 33;      // rows x slots of one window
+constexpr int MAX_PICKS = 8 * 32 * 9;   // rows x slots of one window (8 ranks x 32 rows x 9 slots on an EP receiver)
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -119,21 +119,23 @@ __device__ __forceinline__ float round_bf16_d(double v) {
 }
 
 // Distinct experts (< n_ids) of picks[0..n) in id order -> uids / ucount; per expert its members i (row * 32 + slot,
-// i = row * slots + slot) in order, padded with -1 to maxm. One CTA; picks in shared memory.
+// i = row * slots + slot) in order, padded with -1 to maxm. An expert with more than maxm members takes
+// ceil(count / maxm) consecutive entries (the same id, members in order, maxm an entry): never the case for a window
+// of at most maxm rows, where every expert has at most one member a row. One CTA; picks in shared memory.
 __device__ void group_block(const int* sh_pick, int n, int slots, int n_ids, int* __restrict__ uids,
                             int* __restrict__ ucount, int* __restrict__ members, int maxm, int maxu) {
     __shared__ int warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int per = (n_ids + blockDim.x - 1) / blockDim.x;    // ids a thread (<= 2 with 256 threads, 512 ids)
     int cnt[2] = {0, 0};
-    int used = 0;
+    int used = 0;                                             // entries of this thread's ids
     for (int q = 0; q < per && q < 2; ++q) {
         const int e = threadIdx.x * per + q;
         int c = 0;
         if (e < n_ids)
             for (int i = 0; i < n; ++i) c += sh_pick[i] == e;
         cnt[q] = c;
-        used += c > 0;
+        used += (c + maxm - 1) / maxm;
     }
     int inc = used;
 #pragma unroll
@@ -159,13 +161,21 @@ __device__ void group_block(const int* sh_pick, int n, int slots, int n_ids, int
     for (int q = 0; q < per && q < 2; ++q) {
         if (cnt[q] == 0) continue;
         const int e = threadIdx.x * per + q;
-        if (place < maxu) {
-            uids[place] = e;
-            int j = 0;
-            for (int i = 0; i < n && j < maxm; ++i)
-                if (sh_pick[i] == e) members[place * maxm + j++] = (i / slots) * 32 + (i % slots);
+        int j = 0;                                            // member index within the current entry
+        for (int i = 0; i < n; ++i)
+            if (sh_pick[i] == e) {
+                if (j == maxm) {                              // entry full: the next entry of the same id
+                    ++place;
+                    j = 0;
+                }
+                if (place < maxu) {
+                    if (j == 0) uids[place] = e;
+                    members[place * maxm + j] = (i / slots) * 32 + (i % slots);
+                }
+                ++j;
+            }
+        if (place < maxu)
             for (; j < maxm; ++j) members[place * maxm + j] = -1;
-        }
         ++place;
     }
 }

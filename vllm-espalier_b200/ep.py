@@ -1,0 +1,157 @@
+"""Expert-parallel MoE layer over the ranks of one box (one process a GPU, torch.distributed over NCCL).
+
+The reference runs a MoE layer on one GPU (vllm_espalier/experts.py routed2); this is the sharded form of the same
+layer, with outputs bit-identical to it for every world size:
+
+  * rank q holds routed experts [q E / world, (q + 1) E / world) (contiguous blocks: 128 / 64 / 32 at 2 / 4 / 8 ranks)
+    plus the shared expert; the router and the shared gate are replicated.
+  * each rank routes its own rows with the fused routing kernel (the same bits as on one GPU);
+  * dispatch: every row and its pick list go to every rank (one all_to_all of [world][R][D] bf16 rows and one of
+    [world][R][slots] int32 picks: fixed sizes, so the step is CUDA-graph capturable and the exchange is at most
+    8 x 32 x 4 KiB = 1 MiB a rank);
+  * each rank maps the received picks to its local expert ids (the shared slot is local only on the row's home rank),
+    groups them (an expert with more than 32 members takes several entries) and runs rot_in, the fused gate/up and
+    the fused down kernels on all received rows, producing fp32 y rows per slot;
+  * combine: the y rows go back to their home rank (one all_to_all of [world][R][slots][D] fp32), which sums each
+    row's routed slots in slot order with fp32 fused multiply-adds from 0 (esp_ep_combine): the single-GPU kernel's
+    arithmetic on the same y values, hence the same output bits.
+
+The index logic (local tables, owners, buffer layouts) is in plain torch functions shared by the GPU path and the
+CPU tests (gloo ranks with a stand-in expert function).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import DTYPE, check, ext, lib, stream_ptr
+from . import experts as X
+
+MAXM = 32   # members an entry of the receiver's grouping
+
+
+def expert_range(rank: int, world: int, E: int) -> tuple[int, int]:
+    """Routed experts [e0, e1) held by `rank`."""
+    return rank * E // world, (rank + 1) * E // world
+
+
+def owner_of(e: torch.Tensor, world: int, E: int) -> torch.Tensor:
+    """Rank holding routed expert e (the largest q with q E / world <= e)."""
+    return ((e + 1) * world - 1) // E
+
+
+def local_table(recv_pick: torch.Tensor, rank: int, world: int, E: int, n_routed: int) -> torch.Tensor:
+    """recv_pick int32 [world][R][slots] (global ids, the shared slot = slot n_routed with id E) -> the receiving rank's
+    pick table: local routed ids e - e0 for its experts, nl (the local shared entry) for the shared slot of its own rows
+    only, -1 elsewhere."""
+    e0, e1 = expert_range(rank, world, E)
+    nl = e1 - e0
+    lp = torch.where((recv_pick >= e0) & (recv_pick < e1), recv_pick - e0, torch.full_like(recv_pick, -1))
+    if recv_pick.shape[2] > n_routed:
+        src = torch.arange(world, device=recv_pick.device).view(world, 1)
+        sh = recv_pick[:, :, n_routed]
+        lp[:, :, n_routed] = torch.where((src == rank) & (sh >= 0), torch.full_like(sh, nl), torch.full_like(sh, -1))
+    return lp
+
+
+def dispatch(x: torch.Tensor, pick: torch.Tensor, world: int, group=None):
+    """Every row and its pick list to every rank. Returns (recv_x [world][R][D], recv_pick [world][R][slots])."""
+    import torch.distributed as dist
+    R, D = x.shape
+    send_x = x.unsqueeze(0).expand(world, R, D).contiguous()
+    send_p = pick.unsqueeze(0).expand(world, *pick.shape).contiguous()
+    recv_x, recv_p = torch.empty_like(send_x), torch.empty_like(send_p)
+    dist.all_to_all_single(recv_x, send_x, group=group)
+    dist.all_to_all_single(recv_p, send_p, group=group)
+    return recv_x, recv_p
+
+
+def give_back(y: torch.Tensor, group=None) -> torch.Tensor:
+    """y fp32 [world][R][slots][D] (rows received from each source) -> the same layout indexed by owner on the home
+    rank."""
+    import torch.distributed as dist
+    out = torch.empty_like(y)
+    dist.all_to_all_single(out, y.contiguous(), group=group)
+    return out
+
+
+class EPLayer:
+    """One MoE layer's local share on this rank. `local_experts`: the (gate, up, down) matrices of experts
+    [e0, e1) = expert_range(rank, world, E); `shared`: the shared expert's, `gate_w` its sigmoid-gate weight."""
+
+    def __init__(self, local_experts, shared, gate_w: torch.Tensor, rank: int, world: int, E: int, rows: int = 32,
+                 k: int = 8):
+        e0, e1 = expert_range(rank, world, E)
+        if len(local_experts) != e1 - e0:
+            raise ValueError(f"rank {rank} of {world} holds experts [{e0}, {e1}), got {len(local_experts)}")
+        self.rank, self.world, self.E, self.k = rank, world, E, k
+        self.L = X.prepare(local_experts, shared, gate_w)          # local ids 0..nl-1, the shared entry nl
+        self.nl = e1 - e0
+        self.gate_w = self.L.gate_w
+        dev = gate_w.device
+        D, I = self.L.D, self.L.I
+        self.slots = k + 1
+        self.rows = rows
+        # the home side: routing of this rank's rows (global ids, shared id = E)
+        self.rs = X.Scratch(E, D, I, rows, self.slots, dev)
+        # the expert side: all ranks' rows
+        P = world * rows * self.slots
+        self.P = P
+        self.maxu = min(P, self.nl + 1 + P // MAXM + 1)
+        self.S = X.gateup_splits(D, I, self.slots)
+        self.xg = torch.zeros((P, D), dtype=torch.float16, device=dev)
+        self.xu = torch.zeros((P, D), dtype=torch.float16, device=dev)
+        self.xd = torch.zeros((P, I), dtype=torch.float16, device=dev)
+        self.z = torch.zeros((2 * self.S * P * I,), dtype=torch.float32, device=dev)
+        self.y = torch.zeros((P, D), dtype=torch.float32, device=dev)
+        self.ids = torch.zeros((self.maxu,), dtype=torch.int32, device=dev)
+        self.count = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.members = torch.full((self.maxu, MAXM), -1, dtype=torch.int32, device=dev)
+        self.cnt_gu = torch.zeros((self.maxu * (I // 128),), dtype=torch.int32, device=dev)
+        self.cnt_d = torch.zeros((world * rows * (D // 128),), dtype=torch.int32, device=dev)
+        self.no_w = torch.zeros((P,), dtype=torch.float32, device=dev)
+        self.no_out = torch.empty((world * rows, D), dtype=torch.bfloat16, device=dev)
+
+    def route(self, x: torch.Tensor, gate: torch.Tensor):
+        """Fused routing of this rank's rows -> (pick int32 [R][slots], wts fp32 [R][slots]), global ids."""
+        R = x.shape[0]
+        s = self.rs
+        ids, members = s.window(R)
+        ext().route_group(x, gate, self.gate_w, self.k, self.E, s.logits, s.route_counter, s.pick[:R * self.slots],
+                          s.wts[:R * self.slots], ids, s.count, members)
+        return s.pick[:R * self.slots].view(R, self.slots), s.wts[:R * self.slots].view(R, self.slots)
+
+    def experts(self, recv_x: torch.Tensor, lp: torch.Tensor) -> torch.Tensor:
+        """y fp32 [world][R][slots][D] of the local experts for every received (row, slot) with a local pick."""
+        e = ext()
+        world, R, D = recv_x.shape
+        rows, slots = world * R, self.slots
+        P = rows * slots
+        if R > self.rows:
+            raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
+        L = self.L
+        lpf = lp.reshape(-1)
+        xr = recv_x.view(rows, D)
+        e.group(lpf, self.ids, self.count, self.members, rows, slots, self.nl + 1)
+        e.rot_in(xr, D, lpf, L.suh_g, L.suh_u, self.xg, self.xu, rows, D, slots, self.nl + 1)
+        e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, P, self.S, self.z, self.cnt_gu,
+                     self.xd)
+        e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
+                   self.cnt_d, self.no_out[:rows], None)
+        return self.y[:P].view(world, R, slots, D)
+
+    def forward(self, x: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
+                out_shared: torch.Tensor | None = None, group=None):
+        """x [R, D] bf16/fp16 (this rank's rows), gate [E, D] the router -> (routed sum, shared output), [R, D] in x's
+        dtype, bit-identical to experts.routed2 on one GPU holding every expert."""
+        R, D = x.shape
+        pick, wts = self.route(x, gate)
+        recv_x, recv_p = dispatch(x, pick, self.world, group)
+        lp = local_table(recv_p, self.rank, self.world, self.E, self.k)
+        y = self.experts(recv_x, lp)
+        back = give_back(y, group)
+        out = out if out is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
+        out_shared = out_shared if out_shared is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
+        check(lib().esp_ep_combine(back.data_ptr(), pick.data_ptr(), wts.data_ptr(), out.data_ptr(),
+                                   out_shared.data_ptr(), DTYPE[out.dtype], R, D, self.slots, self.k, self.E,
+                                   self.world, self.rank, stream_ptr(x.device)))
+        return out, out_shared
