@@ -173,8 +173,9 @@ int esp_grouped(const uint16_t* X0, const uint16_t* X1, const int64_t* TP0, cons
 /*
  * Fused gate + up + SwiGLU: xd fp16 [P][I] for every slot with a valid expert, equal to grouped(mats = 2) followed
  * by gateup_epilogue(act_mode 1, no limit). S > 1 splits D in S k-slices whose fp32 partials go to Z
- * ([2][S][P][I]) and are added in slice order by the last of the S to finish; counters (int32, maxu * I / 128,
- * zero and left zero) count the arrivals. No single counterpart: replaces the reference's grouped + gateup_epilogue
+ * ([2][S][P][I]) and are added in slice order by the last of the S to finish; counters (int32, maxu * I / 128 + 1,
+ * zero and left zero) count the arrivals, the last entry hands out the work items (with counters NULL, allowed when
+ * S == 1, items are assigned round robin). No single counterpart: replaces the reference's grouped + gateup_epilogue
  * pair of launches (vllm_espalier/experts.py routed2).
  */
 int esp_moe_gateup(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u,
@@ -186,8 +187,8 @@ int esp_moe_gateup(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, 
 /*
  * Fused down + combine: y fp32 [P][D] per slot, out [rows][D] = the routed slots' sum of w * y in slot order (fp32
  * fused multiply-adds from 0) and out_shared [rows][D] = w * y of the shared slot (slot n_routed, when
- * n_routed < slots), both in out_dtype; rows without a valid slot get zeros. counters: int32, rows * D / 128, zero and
- * left zero. Equals grouped(mats = 1) + down_combine2. No single counterpart: replaces the reference's grouped +
+ * n_routed < slots), both in out_dtype; rows without a valid slot get zeros. counters: int32, rows * D / 128 + 1,
+ * zero and left zero (the arrivals, then the work-item counter). Equals grouped(mats = 1) + down_combine2. No single counterpart: replaces the reference's grouped +
  * down_combine2 pair of launches (vllm_espalier/experts.py routed2).
  */
 int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const int* cb_d, const int* k2_host,

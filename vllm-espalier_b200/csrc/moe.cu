@@ -72,6 +72,7 @@ struct GroupedParams {
     int maxm, slots, K, N, P, S, mats, mode, E;
     float* Z;                      // MODE_Z: [mats][S][P][N]; MODE_GATEUP (S > 1): [2][S][P][N] partials
     int* counters;                 // MODE_GATEUP: [maxu][N/128]; MODE_DOWN: [rows][N/128]; zero, left zero
+    int* work;                     // fused modes: the item counter (after the arrival counters); zero, left zero
     // MODE_GATEUP epilogue
     const __half* svh_g;           // [E][N]
     const __half* svh_u;
@@ -205,6 +206,7 @@ __device__ __forceinline__ void swiglu_store(const GroupedParams& p, int e, int 
 
 // Per work item descriptor, written into shared memory by the producer and read by the consumers.
 struct ItemDesc {
+    int it;                // the work item; -1: no more items for this CTA (an empty stage carries it)
     int e, b, split, mat0, nmats, kt0, nkt, nm;
     int cb0, K0, cb1, K1;
     int rows[32];          // slot index p of each member
@@ -215,6 +217,8 @@ constexpr int NDESC = 16;
 constexpr int MAX_PEND = 1024;     // deferred arrivals a CTA (items a CTA x members an item)
 
 // Work item `it` of MODE: (expert position u, block b, z); z = split (fused modes) or mat * S + split (MODE_Z).
+// The fused modes hand items out dynamically (an atomic counter, from the last expert down: the shared expert, the
+// widest and with the most members, starts first), MODE_Z round robin; sums never depend on which CTA runs an item.
 __device__ __forceinline__ void item_coords(const GroupedParams& p, int it, int NB, int NZ, int& u, int& b, int& z) {
     u = it / (NB * NZ);
     const int r = it - u * NB * NZ;
@@ -238,6 +242,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     __shared__ int s_pend[MAX_PEND][2];      // deferred arrivals: (counter index, item or row code)
     __shared__ int s_npend;
     __shared__ int s_last[MAX_PEND];
+    __shared__ int s_item[NDESC];            // producer 0 -> producer 1: the next item
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NB = p.N / 128;
@@ -245,7 +250,10 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     const int KT = p.K / 16;
     pdl_launch_dependents();
     pdl_wait();
-    const int n_items = p.ucount[0] * NB * NZ;         // grid: one CTA an SM, items round robin
+    const int n_items = p.ucount[0] * NB * NZ;         // grid: one CTA an SM
+    const bool dyn = p.work != nullptr;
+    // deferred arrivals an item adds at most (the producer stops taking items before the table could overflow)
+    const int pend_item = p.mode == MODE_DOWN ? p.maxm : (p.mode == MODE_GATEUP && p.S > 1 ? 1 : 0);
     if (threadIdx.x == 0) {
         for (int i = 0; i < GSTAGES; ++i) {
             mbar_init(&full[i], 32 * GPROD + 1);       // the producers' copy arrivals + the release of descriptors
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             }
         }
     }
-    if ((int)blockIdx.x >= n_items) return;
+    if (!dyn && (int)blockIdx.x >= n_items) return;
 
     if (warp >= GWARPS) {   // ---------------- producers ----------------
         // Producer pw copies the units of position j = pw (mod 2) of every stage: with two matrices (gate, up units
@@ -282,8 +290,43 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
         // memory; producer 0 writes it to shared memory and releases it with the item's stages.
         const int pw = warp - GWARPS;
         const uint32_t sbase = smem_addr(smem);
-        int slot = 0, phase = 0, nstage = 0, di = 0;
-        for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
+        int slot = 0, phase = 0, nstage = 0, di = 0, pend = 0;
+        for (int k = 0;; ++k, di = (di + 1) % NDESC) {
+            int it;
+            if (dyn) {   // producer 0 takes the next item and hands it to producer 1 (64-thread named barrier)
+                if (pw == 0 && lane == 0) {
+                    int t = n_items;
+                    if (pend + pend_item <= MAX_PEND) {
+                        t = atomicAdd(p.work, 1);
+                        if (t == n_items + (int)gridDim.x - 1) *p.work = 0;     // the last fetch of the launch
+                    } else {
+                        atomicAdd(p.work, 1);                                     // count the terminal fetch
+                        t = n_items;
+                    }
+                    s_item[di] = t < n_items ? n_items - 1 - t : -1;
+                }
+                named_sync(2, 32 * GPROD);
+                it = s_item[di];
+                pend += pend_item;
+            } else {
+                it = blockIdx.x + k * (int)gridDim.x;
+                if (it >= n_items) it = -1;
+            }
+            if (it < 0) {   // an empty stage tells the consumers there is nothing more
+                if (pw == 0) {
+                    if (lane == 0) {
+                        desc[di].it = -1;
+                        desc[di].nkt = 0;
+                        desc[di].nmats = 0;
+                        desc[di].nm = 0;
+                    }
+                    __syncwarp();
+                }
+                if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
+                cp_async_arrive(&full[slot]);
+                if (pw == 0 && lane == 0) mbar_arrive(&full[slot]);
+                break;
+            }
             int u, b, z;
             item_coords(p, it, NB, NZ, u, b, z);
             const int e = p.uids[u];
@@ -301,7 +344,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                 ItemDesc& d = desc[di];
                 d.rows[lane] = row;
                 if (lane == 0) {
-                    d.e = e; d.b = b; d.split = split; d.mat0 = mat0; d.nmats = nmats; d.kt0 = kt0; d.nkt = nkt;
+                    d.it = it; d.e = e; d.b = b; d.split = split; d.mat0 = mat0; d.nmats = nmats; d.kt0 = kt0; d.nkt = nkt;
                     d.nm = nm; d.cb0 = p.cb[mat0][e]; d.K0 = p.k2[mat0][e] / 2; d.cb1 = p.cb[mmB][e];
                     d.K1 = p.k2[mmB][e] / 2;
                 }
@@ -355,7 +398,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
     const int g = lane >> 2, t = lane & 3;
     constexpr int CT = GWARPS * 32;
     int slot = 0, phase = 0, di = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x, di = (di + 1) % NDESC) {
+    for (;; di = (di + 1) % NDESC) {
         float acc[2][NTG][4];      // [even/odd unit of this group][token group][4]
 #pragma unroll
         for (int e2 = 0; e2 < 2; ++e2)
@@ -363,9 +406,14 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             for (int q = 0; q < NTG; ++q) acc[e2][q][0] = acc[e2][q][1] = acc[e2][q][2] = acc[e2][q][3] = 0.f;
         const ItemDesc* d = &desc[di];
         int nkt = 0, nmats = 0, ntg = 0, mcb = 0, mK = 0;
+        int item = -1;
         for (int i0 = 0;; i0 += GUPS) {
-            mbar_wait(&full[slot], phase);
+            if (!mbar_wait(&full[slot], phase)) {   // gave up (status recorded): stop taking items
+                item = -1;
+                break;
+            }
             if (i0 == 0) {   // the descriptor is published with the item's first stage
+                item = d->it;
                 nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
                 const bool mB = nmats == 2 && grp == 1;      // with two matrices, group = matrix
                 mcb = mB ? d->cb1 : d->cb0;
@@ -385,6 +433,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             }
             if (i0 + GUPS >= n) break;
         }
+        if (item < 0) break;   // no more items (or a wait gave up)
 
         // ---- the item's sums, even + odd units, into red[matrix][member][column]: with two matrices each group
         //      writes its own; with one, group 0 writes and group 1 adds ----
@@ -412,7 +461,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
         const int e = d->e, b = d->b, nm = d->nm;
         const int n0 = b * 128 + 4 * lane;
         int u, bb, z;
-        item_coords(p, it, NB, NZ, u, bb, z);
+        item_coords(p, item, NB, NZ, u, bb, z);
 
         if (p.mode == MODE_Z) {   // sums of the exact weights: the kernel form times its codebook step
             const float c0 = cb_step(cb0);
@@ -428,7 +477,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                         *reinterpret_cast<const float4*>(red + ((size_t)mi * MP + m) * GRED + 4 * lane);
             if (threadIdx.x == 0) {
                 s_pend[s_npend][0] = u * NB + b;
-                s_pend[s_npend][1] = it;
+                s_pend[s_npend][1] = item;
                 ++s_npend;
             }
         } else if (p.mode == MODE_GATEUP) {   // whole K in this item: the epilogue now
@@ -720,8 +769,10 @@ int launch_grouped(const GroupedParams& p, int ntg, int kmax, int maxu, void* st
     const long long most = (long long)maxu * (p.N / 128) * (p.mode == MODE_Z ? p.mats * p.S : p.S);
     const dim3 grid((unsigned)std::min<long long>(device_sms(), most));
     const long long per_cta = (most + grid.x - 1) / grid.x;
-    ESP_REQUIRE(per_cta * (p.mode == MODE_DOWN ? p.maxm : 1) <= MAX_PEND, ESP_ERR_INVALID,
-                "grouped: %lld items a CTA exceed the deferred-arrival table", per_cta);
+    const int pend_item = p.mode == MODE_DOWN ? p.maxm : 1;
+    // static (MODE_Z): the round-robin share of a CTA; dynamic: every item must fit in the CTAs' tables
+    ESP_REQUIRE(p.work ? most <= (long long)grid.x * (MAX_PEND / pend_item) : per_cta * pend_item <= MAX_PEND,
+                ESP_ERR_INVALID, "grouped: %lld items exceed the deferred-arrival tables", most);
 #define ESP_G(N_)                                                                                   \
     return kmax <= 4 ? launch_grouped_t<N_, 4>(p, grid, stream) : launch_grouped_t<N_, 8>(p, grid, stream);
     switch (ntg) {
@@ -823,6 +874,7 @@ int esp_moe_gateup(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, 
     p.uids = uids; p.ucount = ucount; p.members = members;
     p.maxm = maxm; p.slots = slots; p.K = D; p.N = I; p.P = P; p.S = S; p.mats = 2; p.mode = MODE_GATEUP; p.E = E;
     p.Z = Z; p.counters = counters;
+    p.work = counters ? counters + (size_t)maxu * (I / 128) : nullptr;   // the item counter after the arrivals
     p.svh_g = reinterpret_cast<const __half*>(svh_g);
     p.svh_u = reinterpret_cast<const __half*>(svh_u);
     p.suh_d = reinterpret_cast<const __half*>(suh_d);
@@ -853,6 +905,7 @@ int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const
     p.uids = uids; p.ucount = ucount; p.members = members;
     p.maxm = maxm; p.slots = slots; p.K = I; p.N = D; p.P = rows * slots; p.S = 1; p.mats = 1; p.mode = MODE_DOWN;
     p.E = E; p.counters = counters;
+    p.work = counters + (size_t)rows * (D / 128);                          // the item counter after the arrivals
     p.svh_d = reinterpret_cast<const __half*>(svh_d);
     p.pick = pick; p.wts = wts; p.y = y; p.out = out; p.out_shared = out_shared; p.out_dtype = out_dtype;
     p.n_routed = n_routed;

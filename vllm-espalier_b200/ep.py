@@ -106,8 +106,8 @@ class EPLayer:
         self.ids = torch.zeros((self.maxu,), dtype=torch.int32, device=dev)
         self.count = torch.zeros((1,), dtype=torch.int32, device=dev)
         self.members = torch.full((self.maxu, MAXM), -1, dtype=torch.int32, device=dev)
-        self.cnt_gu = torch.zeros((self.maxu * (I // 128),), dtype=torch.int32, device=dev)
-        self.cnt_d = torch.zeros((world * rows * (D // 128),), dtype=torch.int32, device=dev)
+        self.cnt_gu = torch.zeros((self.maxu * (I // 128) + 1,), dtype=torch.int32, device=dev)
+        self.cnt_d = torch.zeros((world * rows * (D // 128) + 1,), dtype=torch.int32, device=dev)
         self.no_w = torch.zeros((P,), dtype=torch.float32, device=dev)
         self.no_out = torch.empty((world * rows, D), dtype=torch.bfloat16, device=dev)
 

@@ -154,8 +154,9 @@ class Scratch:
         self.ids = torch.zeros((maxu,), dtype=torch.int32, device=device)
         self.count = torch.zeros((1,), dtype=torch.int32, device=device)
         self.members = torch.full((maxu * rows,), -1, dtype=torch.int32, device=device)
-        self.cnt_gu = torch.zeros((maxu * (I // 128),), dtype=torch.int32, device=device)   # gate/up slice arrivals
-        self.cnt_d = torch.zeros((rows * (D // 128),), dtype=torch.int32, device=device)    # per-row slot arrivals
+        # gate/up slice arrivals and per-row slot arrivals, each followed by the launch's work-item counter
+        self.cnt_gu = torch.zeros((maxu * (I // 128) + 1,), dtype=torch.int32, device=device)
+        self.cnt_d = torch.zeros((rows * (D // 128) + 1,), dtype=torch.int32, device=device)
         self.rows, self.slots, self.E = rows, slots, E
 
     def window(self, R: int):
