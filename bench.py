@@ -283,6 +283,118 @@ def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float, rank
             "launches_per_layer": 4 if world == 1 else None, "batches": res}
 
 
+# ---------------------------------------------------------------------------------------------------------------
+# the full synthetic decoder on one GPU. 40 layers, hidden 2048, each a mixer block (the
+# config-2 q/k/v and o projections, 4-bit int5, around a mixer core) and a config-3 MoE layer, with RMSNorms and
+# residual adds; 3:1 DeltaNet : gated-attention blocks; bf16 embedding [248320, 2048]; LM head 2048 -> 248320, 6-bit
+# mcg. The mixer cores (DeltaNet, attention with an fp8 KV cache, MTP) are not on this path: both sides of a parity
+# check use the same stand-in (mixer_core), a fixed elementwise function of the q/k/v projection.
+# ---------------------------------------------------------------------------------------------------------------
+VOCAB = 248320
+RES_SCALE = 0.1
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(torch.bfloat16)
+
+
+def mixer_core(qkv: torch.Tensor, attention: bool) -> torch.Tensor:
+    """Stand-in for the DeltaNet / gated-attention core: [R, 4096 + 512 + 512] -> [R, 4096] bf16."""
+    q, k, v = qkv[:, :O_IN].float(), qkv[:, O_IN:O_IN + KV].float(), qkv[:, O_IN + KV:].float()
+    kk, vv = k.repeat(1, O_IN // KV), v.repeat(1, O_IN // KV)
+    out = q * torch.sigmoid(kk) + vv if attention else torch.tanh(q) * torch.sigmoid(kk) + 0.5 * vv
+    return out.to(torch.bfloat16)
+
+
+def residual(x: torch.Tensor, *ys: torch.Tensor) -> torch.Tensor:
+    acc = x.float()
+    for y in ys:
+        acc = acc + RES_SCALE * y.float()
+    return acc.to(torch.bfloat16)
+
+
+class Decoder:
+    """The config-5 decoder through this library's kernels (dense, routing, grouped experts)."""
+
+    def __init__(self, dev, layers: int = 40, seed: int = 2):
+        __graft_entry__.load_package()
+        from vllm_espalier_b200 import dense as D
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        self.layers, self.dev = layers, dev
+        self.G, self.moe = build_moe(layers, dev, seed=seed + 1)
+        self.embed = torch.randn(VOCAB, HIDDEN, device=dev, generator=gen).to(torch.bfloat16)
+        self.blocks = []
+        for i in range(layers):
+            qkv = D.Dense([Mat(HIDDEN, n, gen, dev) for n in QKV_N])
+            o = D.Dense([Mat(O_IN, HIDDEN, gen, dev)])
+            n1 = (1 + 0.05 * torch.randn(HIDDEN, device=dev, generator=gen)).to(torch.bfloat16)
+            n2 = (1 + 0.05 * torch.randn(HIDDEN, device=dev, generator=gen)).to(torch.bfloat16)
+            self.blocks.append({"qkv": qkv, "o": o, "n1": n1, "n2": n2, "attention": i % 4 == 3})
+        self.final = (1 + 0.05 * torch.randn(HIDDEN, device=dev, generator=gen)).to(torch.bfloat16)
+        self.head = D.Dense([Mat.__new__(Mat).__init_moe__(HIDDEN, VOCAB, 6, 0, gen, dev)])   # grid 0 = mcg
+        self.s = self.G.scratch(self.moe[0][0], 32, MOE_K + 1, dev)
+
+    def head_bytes(self) -> int:
+        return _mat_bytes(self.head.mats[0])
+
+    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        """tokens int64 [R] -> logits bf16 [R, VOCAB] (one decode step)."""
+        G, s = self.G, self.s
+        x = self.embed[tokens]
+        for blk, (L, gate, _, _) in zip(self.blocks, self.moe):
+            h = rmsnorm(x, blk["n1"])
+            core = mixer_core(blk["qkv"].forward(h), blk["attention"])
+            x = residual(x, blk["o"].forward(core))
+            h = rmsnorm(x, blk["n2"])
+            G.route(h, gate, MOE_K, L, s)
+            out, sh = G.routed2(h, None, None, L, s, k=MOE_K)
+            x = residual(x, out, sh)
+        return self.head.forward(rmsnorm(x, self.final))
+
+
+class DecoderStep:
+    def __init__(self, model: Decoder, R: int, dev, seed: int = 3):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.model, self.R = model, R
+        self.tokens = torch.randint(0, VOCAB, (R,), device=dev, generator=g)
+        self.graph = None
+        self.out = None
+
+    def eager(self):
+        self.out = self.model.forward(self.tokens)
+
+    def capture(self):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.eager()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.eager()
+
+    def __call__(self):
+        self.graph.replay() if self.graph is not None else self.eager()
+
+
+def decoder_bench(dev, steps: int, warmup: int, dist) -> dict:
+    model = Decoder(dev)
+    res = {}
+    for R in (1, 8, 32):
+        st = DecoderStep(model, R, dev)
+        st.capture()
+        ms = time_steps(st, steps, warmup, dist, dev)
+        res[str(R)] = {"ms_per_step": ms, "tok_s": R / (ms * 1e-3)}
+        st.graph = None
+    return {"workload": "BASELINE configs[4]: 40-layer synthetic decoder (config-2 projections around stand-in mixer "
+                        "cores, config-3 MoE in every layer, 6-bit mcg LM head to 248320, bf16 embedding), one decode "
+                        "step, graph replay; mixer cores, KV cache and MTP are stand-ins outside this path",
+            "batches": res}
+
+
 def peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -432,11 +544,27 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--moe-layers", type=int, default=8)
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--probe", choices=["dense", "moe"], default=None,
+                    help="no timing: run --probe-iters eager steps of one block / one MoE layer (for ncu captures)")
+    ap.add_argument("--probe-rows", type=int, default=8)
+    ap.add_argument("--probe-iters", type=int, default=3)
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     dist, rank, ws, local = init_dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if a.probe:
+        if a.probe == "dense":
+            st = Step(build_model(2, dev), a.probe_rows, dev)
+        else:
+            G, model = build_moe(1, dev)
+            st = MoEStep(G, model, a.probe_rows, dev)
+        for _ in range(a.probe_iters):
+            st.eager()
+        torch.cuda.synchronize()
+        print(json.dumps({"probe": a.probe, "rows": a.probe_rows, "iters": a.probe_iters}))
+        return
     metric = "decode tok/s + compressed-weight HBM GB/s (% of peak) at batch 1/8/32, 1-8 GPU"
     config = {"workload": f"BASELINE configs[1]: fused dense decode of q/k/v/o blocks, hidden 2048, 4-bit int5, "
                           f"{a.layers} blocks a step (weights > L2, no flush)", "blocks": a.layers,
@@ -503,6 +631,8 @@ def main():
         line["cpu_baseline"] = cpu_baseline(blocks, 1, a.layers, a.cpu_seconds)
     if not a.no_moe:
         line["moe"] = moe_bench(dev, a.moe_layers, max(a.steps // 8, 10), a.warmup, dist, peak, rank, ws)
+    if not a.no_decoder and ws == 1:
+        line["decoder"] = decoder_bench(dev, max(a.steps // 40, 5), a.warmup, dist)
     for st in steps_main.values():
         st.graph = None
     if rank == 0:

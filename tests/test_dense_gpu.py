@@ -96,6 +96,19 @@ def test_config2_block_vs_oracle(dev, M):
         assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
 
 
+@pytest.mark.parametrize("M", [1, 17])
+def test_wide_layer_vs_oracle(dev, M):
+    """A layer with more 128-column blocks (240) than SMs: one range an SM over whole blocks with a partial block at
+    each end, finished through global partial sums by the last CTA to arrive (the path a narrow layer's clusters
+    avoid); 6-bit mcg as the LM head uses."""
+    ms, x, ref = _layer("wide", 256, [240 * 128], 1, 12, M, "bf16", dev)
+    y = D.Dense(ms).forward(x)
+    torch.cuda.synchronize()
+    e, fl = rel_err(f32(y), ref), floor_err(ref, y.dtype)
+    assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
+    assert _lib.device_status() == 0
+
+
 def test_rows_alone_equal_window(dev):
     ms, x, _ = _layer("int5_3bit", 512, [128, 128], 6, 6, 17, "bf16", dev)
     d = D.Dense(ms)

@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -80,6 +81,7 @@ struct DenseParams {
     int* counters;               // [blocks], zero on entry and on exit
     int M, Mp, K, KT, U, G;      // rows, padded rows, inputs, k tiles, units, CTAs (G <= U)
     int NB;                      // 128-column blocks
+    int S;                       // > 1: the S CTAs of a block form a thread-block cluster (block-aligned k-slices)
     float scale;                 // codebook step of the kernel form
 };
 
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
             }
         }
         for (int i = STAGES, slot = 0, phase = 0; i < nst; ++i) {
-            if (!mbar_wait(&empty[slot], phase)) return;
+            if (!mbar_wait(&empty[slot], phase)) break;   // gave up (status recorded)
             fill(i, slot, true, !FUSED, cur);
             cp_async_arrive(&full[slot]);
             if (++slot == STAGES) {
@@ -296,175 +298,198 @@ __global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant
                 phase ^= 1;
             }
         }
-        return;
-    }
+    } else {
 
-    // ---------- consumers: warp w decodes tile w of every unit; even and odd units into separate sums ----------
-    pdl_wait();
-    const int g = lane >> 2, t = lane & 3;
-    const int grp = warp >> 3, wl = warp & 7;
-    constexpr int CT = CWARPS * 32;
+        // ---------- consumers: warp w decodes tile w of every unit; even and odd units into separate sums ----------
+        pdl_wait();
+        const int g = lane >> 2, t = lane & 3;
+        const int grp = warp >> 3, wl = warp & 7;
+        constexpr int CT = CWARPS * 32;
 
-    float acc[2][NTG][4];
-#pragma unroll
-    for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
-
-    if constexpr (FUSED) {   // rows >= M of the rotated activations are zero once and for all
-        const int words = p.xh_chunks * 8 * SLICE_W;
-        for (int i = threadIdx.x; i < words; i += CT) xrot[i] = 0u;
-        named_sync(1, CT);
-    }
-    int pend_bg[2], npend = 0;     // blocks whose partial sums this CTA wrote, completed after the last segment
-    int bg = bg0, kt = kt0, li = 0, j = 0, slot = 0, phase = 0;
-    bool from_zero = kt0 == 0;     // the current segment starts at the block's first k-tile
-    int chunk0 = 0;                // fused: first 128-input chunk held in xrot
-    bool seg_start = true;
-    while (li < n) {
-        if (FUSED && seg_start) {      // rotate this segment's inputs into shared memory
-            const int seg_kt1 = min(p.KT, kt + (n - li));
-            chunk0 = kt >> 3;
-            const int nch = ((seg_kt1 + 7) >> 3) - chunk0;
-            rotate_items<MP>(p, p.s[shard_of(bg, p)].suh, chunk0, nch, warp, lane, reinterpret_cast<__half*>(xrot));
-            named_sync(1, CT);
-            seg_start = false;
-        }
-        if (j == 0) mbar_wait(&full[slot], phase);
-        const uint32_t* st = smem + (size_t)slot * STAGE_W;
-        const int stage_n = min(UPS, n - (li - j));
-        const int run_end = min(stage_n, j + (p.KT - kt));
-        const int kt_at_j = kt;
-        auto slice = [&](int jj) -> const uint32_t* {
-            if constexpr (FUSED) return xrot + (size_t)(kt_at_j + jj - j - 8 * chunk0) * SLICE_W;
-            else return st + UPS * UNIT_W + jj * SLICE_W;
-        };
-        if (j == 0 && run_end == UPS) {      // the common case: a whole stage inside one segment
-#pragma unroll
-            for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
-                const int jj = j2 * GROUPS + grp;
-                uint32_t a[4];
-                decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
-                const uint32_t* xs = slice(jj);
-#pragma unroll
-                for (int q = 0; q < NTG; ++q)
-                    mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
-            }
-        } else {
-            for (int jj = j; jj < run_end; ++jj) {
-                if (GROUPS > 1 && (jj % GROUPS) != grp) continue;
-                uint32_t a[4];
-                decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
-                const uint32_t* xs = slice(jj);
-#pragma unroll
-                for (int q = 0; q < NTG; ++q) mma16816(acc[0][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
-            }
-        }
-        kt += run_end - j;
-        li += run_end - j;
-        j = run_end;
-        if (j == stage_n) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            j = 0;
-            if (++slot == STAGES) {
-                slot = 0;
-                phase ^= 1;
-            }
-        }
-        if (kt != p.KT && li != n) continue;
-
-        // ---- segment end: this warp's 16 columns (even + odd sums) into red[token][column] ----
-        const int col = wl * 16 + g;
-#pragma unroll
-        for (int gi = 0; gi < GROUPS; ++gi) {     // group 0's sums, then group 1's added, in that order
-            if (gi == grp) {
-#pragma unroll
-                for (int q = 0; q < NTG; ++q) {
-                    const int r0 = 8 * q + 2 * t;
-                    float* rr = red + r0 * RED_STRIDE + col;
-                    const float v0 = acc[0][q][0] + acc[1][q][0], v1 = acc[0][q][1] + acc[1][q][1];
-                    const float v2 = acc[0][q][2] + acc[1][q][2], v3 = acc[0][q][3] + acc[1][q][3];
-                    if (gi == 0) {
-                        rr[0] = v0; rr[RED_STRIDE] = v1; rr[8] = v2; rr[RED_STRIDE + 8] = v3;
-                    } else {
-                        rr[0] += v0; rr[RED_STRIDE] += v1; rr[8] += v2; rr[RED_STRIDE + 8] += v3;
-                    }
-                }
-            }
-            if (GROUPS > 1 && gi + 1 < GROUPS) named_sync(1, CT);
-        }
-#pragma unroll
+        float acc[2][NTG][4];
+    #pragma unroll
         for (int e = 0; e < 2; ++e)
-#pragma unroll
+    #pragma unroll
             for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
-        named_sync(1, CT);
 
-        if (from_zero && kt == p.KT) {   // this CTA owns the whole block: finish it now
-            const DShard& S = p.s[shard_of(bg, p)];
-            const int bl = bg - S.nb0;
-            const uint2 sv = load_svh(S, bl, lane);
-            for (int r = warp; r < p.M; r += CWARPS) {
-                const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-                float v[4] = {q.x, q.y, q.z, q.w};
-                finish_store(v, lane, S, bl, r, p, sv);
+        if constexpr (FUSED) {   // rows >= M of the rotated activations are zero once and for all
+            const int words = p.xh_chunks * 8 * SLICE_W;
+            for (int i = threadIdx.x; i < words; i += CT) xrot[i] = 0u;
+            named_sync(1, CT);
+        }
+        int pend_bg[2], npend = 0;     // blocks whose partial sums this CTA wrote, completed after the last segment
+        int bg = bg0, kt = kt0, li = 0, j = 0, slot = 0, phase = 0;
+        bool from_zero = kt0 == 0;     // the current segment starts at the block's first k-tile
+        int chunk0 = 0;                // fused: first 128-input chunk held in xrot
+        bool seg_start = true;
+        while (li < n) {
+            if (FUSED && seg_start) {      // rotate this segment's inputs into shared memory
+                const int seg_kt1 = min(p.KT, kt + (n - li));
+                chunk0 = kt >> 3;
+                const int nch = ((seg_kt1 + 7) >> 3) - chunk0;
+                rotate_items<MP>(p, p.s[shard_of(bg, p)].suh, chunk0, nch, warp, lane, reinterpret_cast<__half*>(xrot));
+                named_sync(1, CT);
+                seg_start = false;
             }
-        } else {                         // partial: store it; the arrival on the block's counter waits for the end
-            float* zs = p.Z + (size_t)(2 * c + (bg == bg0 ? 0 : 1)) * p.M * 128;   // first / last block's slot
-            for (int r = warp; r < p.M; r += CWARPS)
-                *reinterpret_cast<float4*>(zs + r * 128 + 4 * lane) =
-                    *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-            pend_bg[npend++] = bg;
+            if (j == 0) mbar_wait(&full[slot], phase);
+            const uint32_t* st = smem + (size_t)slot * STAGE_W;
+            const int stage_n = min(UPS, n - (li - j));
+            const int run_end = min(stage_n, j + (p.KT - kt));
+            const int kt_at_j = kt;
+            auto slice = [&](int jj) -> const uint32_t* {
+                if constexpr (FUSED) return xrot + (size_t)(kt_at_j + jj - j - 8 * chunk0) * SLICE_W;
+                else return st + UPS * UNIT_W + jj * SLICE_W;
+            };
+            if (j == 0 && run_end == UPS) {      // the common case: a whole stage inside one segment
+    #pragma unroll
+                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                    const int jj = j2 * GROUPS + grp;
+                    uint32_t a[4];
+                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                    const uint32_t* xs = slice(jj);
+    #pragma unroll
+                    for (int q = 0; q < NTG; ++q)
+                        mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                }
+            } else {
+                for (int jj = j; jj < run_end; ++jj) {
+                    if (GROUPS > 1 && (jj % GROUPS) != grp) continue;
+                    uint32_t a[4];
+                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                    const uint32_t* xs = slice(jj);
+    #pragma unroll
+                    for (int q = 0; q < NTG; ++q) mma16816(acc[0][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                }
+            }
+            kt += run_end - j;
+            li += run_end - j;
+            j = run_end;
+            if (j == stage_n) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                j = 0;
+                if (++slot == STAGES) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+            if (kt != p.KT && li != n) continue;
+
+            // ---- segment end: this warp's 16 columns (even + odd sums) into red[token][column] ----
+            const int col = wl * 16 + g;
+    #pragma unroll
+            for (int gi = 0; gi < GROUPS; ++gi) {     // group 0's sums, then group 1's added, in that order
+                if (gi == grp) {
+    #pragma unroll
+                    for (int q = 0; q < NTG; ++q) {
+                        const int r0 = 8 * q + 2 * t;
+                        float* rr = red + r0 * RED_STRIDE + col;
+                        const float v0 = acc[0][q][0] + acc[1][q][0], v1 = acc[0][q][1] + acc[1][q][1];
+                        const float v2 = acc[0][q][2] + acc[1][q][2], v3 = acc[0][q][3] + acc[1][q][3];
+                        if (gi == 0) {
+                            rr[0] = v0; rr[RED_STRIDE] = v1; rr[8] = v2; rr[RED_STRIDE + 8] = v3;
+                        } else {
+                            rr[0] += v0; rr[RED_STRIDE] += v1; rr[8] += v2; rr[RED_STRIDE + 8] += v3;
+                        }
+                    }
+                }
+                if (GROUPS > 1 && gi + 1 < GROUPS) named_sync(1, CT);
+            }
+    #pragma unroll
+            for (int e = 0; e < 2; ++e)
+    #pragma unroll
+                for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
+            named_sync(1, CT);
+
+            if (from_zero && kt == p.KT) {   // this CTA owns the whole block: finish it now
+                const DShard& S = p.s[shard_of(bg, p)];
+                const int bl = bg - S.nb0;
+                const uint2 sv = load_svh(S, bl, lane);
+                for (int r = warp; r < p.M; r += CWARPS) {
+                    const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+                    float v[4] = {q.x, q.y, q.z, q.w};
+                    finish_store(v, lane, S, bl, r, p, sv);
+                }
+            } else if (p.S > 1) {            // partial of a clustered block: stays in red, added after the loop
+            } else {                         // partial: store it; the arrival on the block's counter waits for the end
+                float* zs = p.Z + (size_t)(2 * c + (bg == bg0 ? 0 : 1)) * p.M * 128;   // first / last block's slot
+                for (int r = warp; r < p.M; r += CWARPS)
+                    *reinterpret_cast<float4*>(zs + r * 128 + 4 * lane) =
+                        *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+                pend_bg[npend++] = bg;
+            }
+            named_sync(1, CT);   // red (and the rotation buffer) are reused by the next segment
+            if (kt == p.KT) {
+                kt = 0;
+                ++bg;
+                from_zero = true;
+            }
+            seg_start = true;
         }
-        named_sync(1, CT);   // red (and the rotation buffer) are reused by the next segment
-        if (kt == p.KT) {
-            kt = 0;
-            ++bg;
-            from_zero = true;
+
+        if (npend) {
+            named_sync(1, CT);                 // every partial of this CTA is stored
+            if (threadIdx.x < npend) {
+                const int b = pend_bg[threadIdx.x];
+                const int nc = cta_of(b * p.KT + p.KT - 1, p) - cta_of(b * p.KT, p) + 1;
+                s_lastv[threadIdx.x] = arrive_acq_rel(&p.counters[b]) == nc - 1;   // publishes / sees the partials
+            }
+            named_sync(1, CT);
+            for (int pi = 0; pi < npend; ++pi) {
+                if (!s_lastv[pi]) continue;
+                const int b = pend_bg[pi];
+                const DShard& S = p.s[shard_of(b, p)];
+                const int bl = b - S.nb0;
+                const uint2 sv = load_svh(S, bl, lane);
+                // the block's CTAs, added in k order; only the first can hold it as its last block (slot 2c + 1)
+                const int c_lo = cta_of(b * p.KT, p), c_hi = cta_of(b * p.KT + p.KT - 1, p);
+                const int lo_slot = 2 * c_lo + (range_start(c_lo, p) < b * p.KT ? 1 : 0);
+                for (int r = warp; r < p.M; r += CWARPS) {
+                    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int c8 = c_lo; c8 <= c_hi; c8 += 8) {
+                        float4 q[8];
+    #pragma unroll
+                        for (int d = 0; d < 8; ++d) {
+                            const int cc = c8 + d;
+                            const int slot = cc == c_lo ? lo_slot : 2 * cc;
+                            q[d] = cc <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)slot * p.M + r) * 128 +
+                                                                                       4 * lane))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+    #pragma unroll
+                        for (int d = 0; d < 8; ++d)
+                            if (c8 + d <= c_hi) {
+                                sum.x += q[d].x; sum.y += q[d].y; sum.z += q[d].z; sum.w += q[d].w;
+                            }
+                    }
+                    float v[4] = {sum.x, sum.y, sum.z, sum.w};
+                    finish_store(v, lane, S, bl, r, p, sv);
+                }
+                if (threadIdx.x == 0) p.counters[b] = 0;
+            }
         }
-        seg_start = true;
+
     }
 
-    if (npend) {
-        named_sync(1, CT);                 // every partial of this CTA is stored
-        if (threadIdx.x < npend) {
-            const int b = pend_bg[threadIdx.x];
-            const int nc = cta_of(b * p.KT + p.KT - 1, p) - cta_of(b * p.KT, p) + 1;
-            s_lastv[threadIdx.x] = arrive_acq_rel(&p.counters[b]) == nc - 1;   // publishes / sees the partials
-        }
-        named_sync(1, CT);
-        for (int pi = 0; pi < npend; ++pi) {
-            if (!s_lastv[pi]) continue;
-            const int b = pend_bg[pi];
-            const DShard& S = p.s[shard_of(b, p)];
-            const int bl = b - S.nb0;
-            const uint2 sv = load_svh(S, bl, lane);
-            // the block's CTAs, added in k order; only the first can hold it as its last block (slot 2c + 1)
-            const int c_lo = cta_of(b * p.KT, p), c_hi = cta_of(b * p.KT + p.KT - 1, p);
-            const int lo_slot = 2 * c_lo + (range_start(c_lo, p) < b * p.KT ? 1 : 0);
-            for (int r = warp; r < p.M; r += CWARPS) {
+    if (p.S > 1) {   // the block's S CTAs (one cluster, rank = k-slice) add their partials in rank order
+        cluster_sync_all();
+        if (warp < CWARPS) {
+            const int rank = (int)cluster_rank();
+            const DShard& Sd = p.s[shard_of(bg0, p)];
+            const int bl = bg0 - Sd.nb0;
+            const uint2 sv = load_svh(Sd, bl, lane);
+            for (int r = rank + p.S * warp; r < p.M; r += p.S * CWARPS) {
+                const float* rr = red + r * RED_STRIDE + 4 * lane;
                 float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int c8 = c_lo; c8 <= c_hi; c8 += 8) {
-                    float4 q[8];
-#pragma unroll
-                    for (int d = 0; d < 8; ++d) {
-                        const int cc = c8 + d;
-                        const int slot = cc == c_lo ? lo_slot : 2 * cc;
-                        q[d] = cc <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)slot * p.M + r) * 128 +
-                                                                                   4 * lane))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int d = 0; d < 8; ++d)
-                        if (c8 + d <= c_hi) {
-                            sum.x += q[d].x; sum.y += q[d].y; sum.z += q[d].z; sum.w += q[d].w;
-                        }
+                for (int q = 0; q < p.S; ++q) {
+                    const float4 v = ld_cluster_f4(rr, (uint32_t)q);
+                    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
                 }
-                float v[4] = {sum.x, sum.y, sum.z, sum.w};
-                finish_store(v, lane, S, bl, r, p, sv);
+                float v4[4] = {sum.x, sum.y, sum.z, sum.w};
+                finish_store(v4, lane, Sd, bl, r, p, sv);
             }
-            if (threadIdx.x == 0) p.counters[b] = 0;
         }
+        cluster_sync_all();   // no CTA leaves while another still reads its shared memory
     }
 }
 
@@ -526,8 +551,17 @@ size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks) {
 
 constexpr size_t SMEM_LIMIT = 200 * 1024;
 
+// ESPALIER_DENSE_CLUSTER (default 1): finish split blocks inside a thread-block cluster (0: through global partials).
+bool cluster_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("ESPALIER_DENSE_CLUSTER");
+        return !(v && (v[0] == '0' || v[0] == 'f' || v[0] == 'F'));
+    }();
+    return on;
+}
+
 template <int CB, int K, int NTG, bool FUSED>
-int launch_dense(const DenseParams& p, void* stream) {
+int launch_dense(DenseParams p, void* stream) {
     auto kern = dense_kernel<CB, K, NTG, FUSED>;
     const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks);
     static size_t opted = 0;
@@ -535,6 +569,36 @@ int launch_dense(const DenseParams& p, void* stream) {
         if (int rc = allow_smem(kern, FUSED ? SMEM_LIMIT : smem)) return rc;
         opted = FUSED ? SMEM_LIMIT : smem;
     }
+    if (p.S > 1) {   // one cluster a block, if at least one such cluster fits on the device
+        static bool nonportable = false;
+        if (p.S > 8 && !nonportable) {
+            if (cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeNonPortableClusterSizeAllowed,
+                                     1) != cudaSuccess) {
+                cudaGetLastError();
+                p.S = 0;
+            } else {
+                nonportable = true;
+            }
+        }
+        if (p.S > 1) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(p.G);
+            cfg.blockDim = dim3(THREADS);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = static_cast<unsigned>(p.S);
+            at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1) {
+                cudaGetLastError();
+                p.S = 0;
+            }
+        }
+    }
+    if (p.S > 1) return launch_cluster(kern, dim3(p.G), dim3(THREADS), smem, stream, true, p.S, p);
     return launch(kern, dim3(p.G), dim3(THREADS), smem, stream, true, p);
 }
 
@@ -620,6 +684,9 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
         p.G = nbt >= sms ? sms : nbt * std::min(sms / nbt, p.KT);
     }
     ESP_REQUIRE((long long)p.U * p.G < (1ll << 31), ESP_ERR_INVALID, "esp_dense: layer too large (%d units)", p.U);
+    // k-slices of a block finish inside one thread-block cluster when there are 2..16 of them (the limit of a
+    // non-portable cluster on this GPU)
+    p.S = (nbt < p.G && cluster_enabled() && p.G / nbt >= 2 && p.G / nbt <= 16) ? p.G / nbt : 0;
     p.scale = cb_step(cb);
     p.Z = z;
     const size_t zneed = (size_t)2 * p.G * m * 128 * 4;

@@ -49,6 +49,29 @@ int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* s
     return ESP_OK;
 }
 
+// The same with a thread-block cluster of `cluster` CTAs along x (cluster > 1; the grid is a multiple of it).
+template <typename... KArgs, typename... Args>
+int launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, bool pdl, int cluster,
+                   Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (pdl && pdl_enabled()) ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return set_error(ESP_ERR_CUDA, "cluster kernel launch: %s", cudaGetErrorString(e));
+    return ESP_OK;
+}
+
 // Opt a kernel into more than 48 KB of dynamic shared memory (once per kernel).
 template <typename K>
 int allow_smem(K kernel, size_t bytes) {
