@@ -339,16 +339,19 @@ class Decoder:
     def head_bytes(self) -> int:
         return _mat_bytes(self.head.mats[0])
 
-    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
-        """tokens int64 [R] -> logits bf16 [R, VOCAB] (one decode step)."""
+    def forward(self, tokens: torch.Tensor, picks: list | None = None) -> torch.Tensor:
+        """tokens int64 [R] -> logits bf16 [R, VOCAB] (one decode step); `picks` collects each layer's routing."""
         G, s = self.G, self.s
         x = self.embed[tokens]
+        R = tokens.shape[0]
         for blk, (L, gate, _, _) in zip(self.blocks, self.moe):
             h = rmsnorm(x, blk["n1"])
             core = mixer_core(blk["qkv"].forward(h), blk["attention"])
             x = residual(x, blk["o"].forward(core))
             h = rmsnorm(x, blk["n2"])
             G.route(h, gate, MOE_K, L, s)
+            if picks is not None:
+                picks.append(s.pick[:R * (MOE_K + 1)].view(R, MOE_K + 1).clone())
             out, sh = G.routed2(h, None, None, L, s, k=MOE_K)
             x = residual(x, out, sh)
         return self.head.forward(rmsnorm(x, self.final))
