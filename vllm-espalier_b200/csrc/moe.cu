@@ -175,11 +175,20 @@ __device__ __forceinline__ void dispatch_units(int cb, int K, const uint32_t* st
 
 // The gate/up epilogue of one member row's 4 columns of this lane (experts.cu:120-162, act_mode 1): sums times the
 // codebook steps, H, * h * svh, silu(g) * u, * suh_d (never contracted into the butterfly), H, * h -> fp16 xd.
-__device__ __forceinline__ void swiglu_store(const GroupedParams& p, int e, int n0, int pm, float cg, float cu,
-                                             float (&gv)[4], float (&uv)[4], int lane) {
-    const __half* svg = p.svh_g + (size_t)e * p.N + n0;
-    const __half* svu = p.svh_u + (size_t)e * p.N + n0;
-    const __half* sud = p.suh_d + (size_t)e * p.N + n0;
+// The lane's 4 fp16 scales of a 128-column block (8 bytes), loaded ahead of the epilogue that needs them.
+struct Scales4 {
+    uint2 g, u, d;
+};
+__device__ __forceinline__ uint2 ld_scales4(const __half* v, int e, int N, int n0) {
+    return *reinterpret_cast<const uint2*>(v + (size_t)e * N + n0);
+}
+__device__ __forceinline__ float scale_at(const uint2& s, int j) {
+    const uint32_t w = j < 2 ? s.x : s.y;
+    return __half2float(__ushort_as_half((unsigned short)((j & 1) ? (w >> 16) : (w & 0xffffu))));
+}
+
+__device__ __forceinline__ void swiglu_store(const GroupedParams& p, const Scales4& sc, int n0, int pm, float cg,
+                                             float cu, float (&gv)[4], float (&uv)[4], int lane) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         gv[j] *= cg;
@@ -190,10 +199,10 @@ __device__ __forceinline__ void swiglu_store(const GroupedParams& p, int e, int 
     float v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const float gg = gv[j] * HAD_SCALE * __half2float(svg[j]);
-        const float uu = uv[j] * HAD_SCALE * __half2float(svu[j]);
+        const float gg = gv[j] * HAD_SCALE * scale_at(sc.g, j);
+        const float uu = uv[j] * HAD_SCALE * scale_at(sc.u, j);
         const float act = gg / (1.f + expf(-gg)) * uu;
-        v[j] = __fmul_rn(act, __half2float(sud[j]));
+        v[j] = __fmul_rn(act, scale_at(sc.d, j));
     }
     fwht128(v, lane);
     const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
@@ -407,6 +416,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
         const ItemDesc* d = &desc[di];
         int nkt = 0, nmats = 0, ntg = 0, mcb = 0, mK = 0;
         int item = -1;
+        Scales4 sc{};                 // the epilogue's scales, loaded with the item's first stage (latency hidden)
         for (int i0 = 0;; i0 += GUPS) {
             if (!mbar_wait(&full[slot], phase)) {   // gave up (status recorded): stop taking items
                 item = -1;
@@ -418,6 +428,16 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                 const bool mB = nmats == 2 && grp == 1;      // with two matrices, group = matrix
                 mcb = mB ? d->cb1 : d->cb0;
                 mK = mB ? d->K1 : d->K0;
+                if (item >= 0) {
+                    const int n0s = d->b * 128 + 4 * lane;
+                    if (p.mode == MODE_DOWN) {
+                        sc.d = ld_scales4(p.svh_d, d->e, p.N, n0s);
+                    } else if (p.mode == MODE_GATEUP && p.S == 1) {
+                        sc.g = ld_scales4(p.svh_g, d->e, p.N, n0s);
+                        sc.u = ld_scales4(p.svh_u, d->e, p.N, n0s);
+                        sc.d = ld_scales4(p.suh_d, d->e, p.N, n0s);
+                    }
+                }
             }
             const int n = nmats * nkt;
             const uint32_t* st = smem + (size_t)slot * STAGE_W;
@@ -458,7 +478,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             if (nmats == 2) break;
         }
         const int cb0 = d->cb0, cb1 = d->cb1;
-        const int e = d->e, b = d->b, nm = d->nm;
+        const int b = d->b, nm = d->nm;
         const int n0 = b * 128 + 4 * lane;
         int u, bb, z;
         item_coords(p, item, NB, NZ, u, bb, z);
@@ -485,20 +505,20 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                 const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
                 const float4 c4 = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
                 float gv[4] = {a.x, a.y, a.z, a.w}, uv[4] = {c4.x, c4.y, c4.z, c4.w};
-                swiglu_store(p, e, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
+                swiglu_store(p, sc, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
             }
         } else {   // MODE_DOWN: y for this block; row arrivals after the last item
             const float cd = cb_step(cb0);
-            const __half* svd = p.svh_d + (size_t)e * p.N + n0;
+
             for (int m = warp; m < nm; m += GWARPS) {
                 const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
                 float v[4] = {a.x * cd, a.y * cd, a.z * cd, a.w * cd};
                 fwht128(v, lane);
                 float4 o;
-                o.x = v[0] * HAD_SCALE * __half2float(svd[0]);
-                o.y = v[1] * HAD_SCALE * __half2float(svd[1]);
-                o.z = v[2] * HAD_SCALE * __half2float(svd[2]);
-                o.w = v[3] * HAD_SCALE * __half2float(svd[3]);
+                o.x = v[0] * HAD_SCALE * scale_at(sc.d, 0);
+                o.y = v[1] * HAD_SCALE * scale_at(sc.d, 1);
+                o.z = v[2] * HAD_SCALE * scale_at(sc.d, 2);
+                o.w = v[3] * HAD_SCALE * scale_at(sc.d, 3);
                 *reinterpret_cast<float4*>(p.y + (size_t)d->rows[m] * p.N + n0) = o;
             }
             if (threadIdx.x < nm) {
@@ -539,6 +559,8 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             const int e = p.uids[u];
             const float cg = cb_step(p.cb[0][e]), cu = cb_step(p.cb[1 % p.mats][e]);
             const int n0 = b * 128 + 4 * lane;
+            const Scales4 dsc{ld_scales4(p.svh_g, e, p.N, n0), ld_scales4(p.svh_u, e, p.N, n0),
+                              ld_scales4(p.suh_d, e, p.N, n0)};   // issued with the partial sums' loads
             for (int m = warp; m < p.maxm; m += GWARPS) {
                 const int code = p.members[u * p.maxm + m];
                 if (code < 0) continue;
@@ -551,7 +573,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                     su.x += c4.x; su.y += c4.y; su.z += c4.z; su.w += c4.w;
                 }
                 float gv[4] = {sg.x, sg.y, sg.z, sg.w}, uv[4] = {su.x, su.y, su.z, su.w};
-                swiglu_store(p, e, n0, pm, cg, cu, gv, uv, lane);
+                swiglu_store(p, dsc, n0, pm, cg, cu, gv, uv, lane);
             }
             if (threadIdx.x == 0) p.counters[s_pend[pi][0]] = 0;
         } else {                        // MODE_DOWN: combine the row's slots in slot order
