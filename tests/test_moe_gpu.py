@@ -226,6 +226,38 @@ def test_rows_alone_equal_window_and_graph(dev, small_moe):
     assert torch.equal(og, out) and torch.equal(sg, sh)
 
 
+def test_skipped_picks_and_empty_rows(dev, small_moe):
+    """Picks outside [0, E) are skipped (the reference's rule); a row whose routed picks are all skipped gets a zero
+    routed sum and keeps its shared-expert output; the other rows are unchanged bit for bit."""
+    experts_np, xb, pick, wts, gate_w, L = small_moe
+    R, k = pick.shape
+    s = G.scratch(L, 32, k + 1, dev)
+    x = bf(xb, dev)
+    pk, wt = torch.from_numpy(pick).to(dev), torch.from_numpy(wts).to(dev)
+    out, sh = G.routed2(x, pk, wt, L, s)
+    out, sh = out.clone(), sh.clone()
+    pk2 = pk.clone()
+    pk2[1, :] = -1                                   # row 1: every routed pick skipped
+    pk2[2, 0] = C.MOE_E + 5                          # row 2: one pick out of range
+    o2, s2 = G.routed2(x, pk2, wt, L, s)
+    torch.cuda.synchronize()
+    assert torch.equal(o2[0], out[0]) and torch.equal(o2[3], out[3])
+    assert bool((o2[1] == 0).all()) and torch.equal(s2[1], sh[1])
+    routed, _ = _oracle_moe(experts_np, xb[2:3], pick[2:3, 1:], wts[2:3, 1:], gate_w, k - 1)
+    e = rel_err(f32(o2[2:3]), routed)
+    assert e < 1e-2, f"row with a skipped pick: max rel err {e:.3e}"
+    assert _lib.device_status() == 0
+    assert int(s.cnt_gu.abs().sum()) == 0 and int(s.cnt_d.abs().sum()) == 0
+
+
+def test_empty_calls_return_ok(dev):
+    lib = _lib.lib()
+    null = None
+    assert lib.esp_rot_in(16, 1, 2048, 16, 16, 16, 16, 16, 0, 2048, 9, 256, null) == 0   # rows = 0: nothing to do
+    assert lib.esp_combine(16, 16, 16, 0, 2048, 9, null) == 0
+    assert lib.esp_ep_combine(16, 16, 16, 16, null, 1, 0, 2048, 9, 8, 256, 2, 0, null) == 0
+
+
 def _config3_layer(dev, seed=0):
     """256 routed experts 2048 -> 512 -> 2048 with widths 1/2/3 bits (p = .3/.5/.2; 1-2 bit E2M1,
     3 bit int5) and one 4-bit int6 shared expert; router bf16 [256, 2048] N(0, 1/sqrt(2048)); shared gate [2048]."""

@@ -6,8 +6,8 @@ layer, with outputs bit-identical to it for every world size:
   * rank q holds routed experts [q E / world, (q + 1) E / world) (contiguous blocks: 128 / 64 / 32 at 2 / 4 / 8 ranks)
     plus the shared expert; the router and the shared gate are replicated.
   * each rank routes its own rows with the fused routing kernel (the same bits as on one GPU);
-  * dispatch: every row and its pick list go to every rank (one all_to_all of [world][R][D] bf16 rows and one of
-    [world][R][slots] int32 picks: fixed sizes, so the step is CUDA-graph capturable and the exchange is at most
+  * dispatch: every row and its pick list go to every rank in one all_to_all ([world][R][2 D + 4 slots] bytes: the
+    bf16 row, then its int32 picks; fixed sizes, so the step is CUDA-graph capturable and the exchange is at most
     8 x 32 x 4 KiB = 1 MiB a rank);
   * each rank maps the received picks to its local expert ids (the shared slot is local only on the row's home rank),
     groups them (an expert with more than 32 members takes several entries) and runs rot_in, the fused gate/up and
@@ -54,15 +54,19 @@ def local_table(recv_pick: torch.Tensor, rank: int, world: int, E: int, n_routed
 
 
 def dispatch(x: torch.Tensor, pick: torch.Tensor, world: int, group=None):
-    """Every row and its pick list to every rank. Returns (recv_x [world][R][D], recv_pick [world][R][slots])."""
+    """Every row and its pick list to every rank, in one collective: a row travels as the bytes of its D values
+    followed by those of its int32 picks. Returns (recv_x [world][R][D] (a strided view), recv_pick
+    [world][R][slots])."""
     import torch.distributed as dist
     R, D = x.shape
-    send_x = x.unsqueeze(0).expand(world, R, D).contiguous()
-    send_p = pick.unsqueeze(0).expand(world, *pick.shape).contiguous()
-    recv_x, recv_p = torch.empty_like(send_x), torch.empty_like(send_p)
-    dist.all_to_all_single(recv_x, send_x, group=group)
-    dist.all_to_all_single(recv_p, send_p, group=group)
-    return recv_x, recv_p
+    slots = pick.shape[1]
+    nb = x.element_size() * D
+    row = torch.cat([x.contiguous().view(torch.uint8).view(R, nb), pick.contiguous().view(torch.uint8).view(R, 4 * slots)],
+                    1)                                         # bytes: neither NCCL nor gloo has a 16-bit integer type
+    send = row.unsqueeze(0).expand(world, R, nb + 4 * slots).contiguous()
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv[:, :, :nb].view(x.dtype), recv[:, :, nb:].contiguous().view(torch.int32)
 
 
 def give_back(y: torch.Tensor, group=None) -> torch.Tensor:
@@ -130,9 +134,9 @@ class EPLayer:
             raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
         L = self.L
         lpf = lp.reshape(-1)
-        xr = recv_x.view(rows, D)
+        stride = recv_x.stride(1)                 # rows of the packed dispatch buffer: D values, then the picks
         e.group(lpf, self.ids, self.count, self.members, rows, slots, self.nl + 1)
-        e.rot_in(xr, D, lpf, L.suh_g, L.suh_u, self.xg, self.xu, rows, D, slots, self.nl + 1)
+        e.rot_in(recv_x, stride, lpf, L.suh_g, L.suh_u, self.xg, self.xu, rows, D, slots, self.nl + 1)
         e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, P, self.S, self.z, self.cnt_gu,
                      self.xd)
         e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
