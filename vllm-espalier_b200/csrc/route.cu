@@ -53,16 +53,25 @@ __device__ __forceinline__ void add_chunk(const uint4& a4, const float (&wf)[8],
     for (int q = 0; q < 8; ++q) s[q] = __dadd_rn(s[q], (double)__fmul_rn(to_f<T>(a[q]), wf[q]));
 }
 
+constexpr int MAXC = 8;   // 8-value chunks a lane keeps in registers (H <= 2048)
+
+// The lane's chunks of a weight row: loaded before the kernel waits for the previous one (weights are not its output).
+template <typename T>
+__device__ __forceinline__ void load_w(const T* __restrict__ w, int H, int lane, uint4 (&uw)[MAXC]) {
+    const int nc = (H - 8 * lane + 255) / 256;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+        if (i < nc) uw[i] = *reinterpret_cast<const uint4*>(w + 8 * lane + 256 * i);
+}
+
 template <typename T>
 __device__ __forceinline__ void logits64(const T* __restrict__ x, long long x_stride, int nr, const T* __restrict__ w,
-                                         int H, int lane, double (&acc)[RB]) {
-    constexpr int MAXC = 8;
-    uint4 uw[MAXC], ux[RB][MAXC];
+                                         const uint4 (&uw)[MAXC], int H, int lane, double (&acc)[RB]) {
+    uint4 ux[RB][MAXC];
     const int nc = (H - 8 * lane + 255) / 256;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i)
         if (i < nc) {
-            uw[i] = *reinterpret_cast<const uint4*>(w + 8 * lane + 256 * i);
 #pragma unroll
             for (int r = 0; r < RB; ++r)
                 if (r < nr) ux[r][i] = *reinterpret_cast<const uint4*>(x + (size_t)r * x_stride + 8 * lane + 256 * i);
@@ -254,18 +263,20 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
     __shared__ int last;
     __shared__ int sh_pick[MAX_PICKS];
     pdl_launch_dependents();
-    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int has = shared_id >= 0;
     const int C = E + has;                 // logit columns: experts, then the shared gate
     const int slots = k + has;
     const int c = blockIdx.x * RW + warp;      // a warp a (logit column, RB rows)
     const int r0 = blockIdx.y * RB;
+    const T* w = c < E ? gate + (size_t)c * H : sgate;
+    uint4 uw[MAXC];
+    if (c < C) load_w<T>(w, H, lane, uw);      // the router's weights overlap the previous kernel's tail
+    pdl_wait();
     if (c < C) {
-        const T* w = c < E ? gate + (size_t)c * H : sgate;
         const int nr = min(RB, R - r0);
         double acc[RB];
-        logits64<T>(x + (size_t)r0 * x_stride, x_stride, nr, w, H, lane, acc);
+        logits64<T>(x + (size_t)r0 * x_stride, x_stride, nr, w, uw, H, lane, acc);
 #pragma unroll
         for (int r = 0; r < RB; ++r)
             if (r < nr && lane == 0) logits[(size_t)(r0 + r) * C + c] = c < E ? round_bf16_d(acc[r]) : (float)acc[r];
@@ -308,17 +319,16 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
         for (int t = 0; t < k; ++t) sum += __shfl_sync(0xffffffffu, pt, t);
         if (lane < k) {
             pick_out[r * slots + lane] = my_id;
+            sh_pick[r * slots + lane] = my_id;
             wts_out[r * slots + lane] = pt / sum;
         }
         if (has && lane == 0) {
             pick_out[r * slots + k] = shared_id;
+            sh_pick[r * slots + k] = shared_id;
             wts_out[r * slots + k] = 1.f / (1.f + expf(-__ldcg(lr + E)));
         }
     }
-    __syncthreads();
-    const int n = R * slots;
-    for (int i = threadIdx.x; i < n; i += RT) sh_pick[i] = pick_out[i];
-    __syncthreads();
+    __syncthreads();   // the picks are in sh_pick (written beside pick_out above)
     group_distinct(sh_pick, R, slots, E + has, uids, ucount, members, maxm, maxu);
     if (threadIdx.x == 0) *counter = 0;
 }
