@@ -198,6 +198,22 @@ int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const
                  void* stream);
 
 /*
+ * esp_moe_gateup followed by esp_moe_down in one persistent launch, with the same output bits: gate/up work items are
+ * handed out first, a down item starts once its expert's SwiGLU rows are complete (a readiness counter, bounded wait),
+ * and a finisher warp does the slice sums, SwiGLU and row combines as their last arrivals land. Tables k2_host /
+ * cb_host are [3][E] (gate, up, down). counters: int32, esp_moe_layer_counters(maxu, rows, D, I) entries, zero before
+ * the first call and left zero. No single counterpart in the reference (its routed2 runs 4-5 launches for this).
+ */
+int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u, const int64_t* tp_d,
+                  const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g, const int* cb_u, const int* cb_d,
+                  const int* k2_host, const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u,
+                  const uint16_t* suh_d, const uint16_t* svh_d, const int* uids, const int* ucount, const int* members,
+                  int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed, int rows, int D, int I,
+                  int S, float* Z, uint16_t* xd, float* y, int* counters, void* out, void* out_shared, int out_dtype,
+                  void* stream);
+size_t esp_moe_layer_counters(int maxu, int rows, int D, int I);
+
+/*
  * xd fp16 [P][N] from the gate / up partial sums Z [2][SK][P][N] (act_mode 0: bf16-rounded SwiGLU with `limit`,
  * 1: fp32 SwiGLU).
  * Replaces ext().gateup_epilogue(Z, pick, svh_g, svh_u, suh_d, xd, rows, P, N, SK, slots, E, limit, act_mode)

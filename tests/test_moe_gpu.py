@@ -299,3 +299,26 @@ def test_config3_layer_with_fused_routing(dev, R):
         e = rel_err(f32(got), want)
         fl = rel_err(C.bf16_to_f32(C.bf16_bits(want)), want)
         assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
+
+
+@pytest.mark.parametrize("R", [1, 5, 32])
+def test_one_launch_layer_equals_two_launches(dev, monkeypatch, R):
+    """The one-launch layer (gate/up, SwiGLU, down and the per-row combine in one persistent kernel, ready flags
+    between the phases) gives the two-launch pipeline's bits, and leaves its counters and flags zero."""
+    ex_np, gate_b, sgate_b = _config3_layer(dev, seed=1)
+    mats = build(ex_np, dev)
+    L = G.prepare(mats[:-1], mats[-1], bf(sgate_b, dev))
+    k = 8
+    s = G.scratch(L, 32, k + 1, dev)
+    x = bf(C.activations(("one-launch", R), R, 2048), dev)
+    G.route(x, bf(gate_b, dev), k, L, s)
+    monkeypatch.setattr(G, "MOE_ONE_LAUNCH", False)
+    a, b = G.routed2(x, None, None, L, s, k=k)
+    a, b = a.clone(), b.clone()
+    monkeypatch.setattr(G, "MOE_ONE_LAUNCH", True)
+    for _ in range(3):                               # repeated: flags and counters must come back to zero
+        o, sh = G.routed2(x, None, None, L, s, k=k)
+        torch.cuda.synchronize()
+        assert torch.equal(o, a) and torch.equal(sh, b)
+    assert _lib.device_status() == 0
+    assert int(s.cnt_layer.abs().sum()) == 0

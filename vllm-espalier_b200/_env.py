@@ -14,5 +14,6 @@ def flag(name: str, default: str = "1") -> bool:
 FUSED_DENSE = flag("ESPALIER_FUSED_DENSE")            # one launch per vLLM layer
 GROUPED_EXPERTS = flag("ESPALIER_GROUPED_EXPERTS")    # grouped MoE pipeline
 FUSED_ROUTING = flag("ESPALIER_FUSED_ROUTING")        # fused router GEMV + top-k + grouping
+MOE_ONE_LAUNCH = flag("ESPALIER_MOE_FUSED")          # gate/up and down of the experts in one launch (this library)
 PREFILL = env("ESPALIER_PREFILL_MODE", "chunk")       # chunk | gemm
 DEBUG_SHARED_FOLD = flag("ESPALIER_DEBUG_SHARED_FOLD", "0")

@@ -56,6 +56,9 @@ SIGNATURES = {
     "esp_down_combine": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, P]),
     "esp_combine": (I, [P, P, P, I, I, I, P]),
     "esp_ep_combine": (I, [P, P, P, P, P, I, I, I, I, I, I, I, I, P]),
+    "esp_moe_layer": (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P, P, I, I, P, P, I, I, I, I, I, I,
+                          P, P, P, P, P, P, I, P]),
+    "esp_moe_layer_counters": (S, [I, I, I, I]),
     "esp_dense_z_bytes": (S, [I]),
 }
 
@@ -279,6 +282,19 @@ class _Ext:
                                    L.svh_u.data_ptr(), L.suh_d.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
                                    members.data_ptr(), uids.numel(), members.size(1), slots, P, L.D, L.I, S,
                                    z.data_ptr(), counters.data_ptr(), xd.data_ptr(), stream_ptr(xg.device)))
+
+    @staticmethod
+    def moe_layer(xg, xu, L, uids, ucount, members, pick, wts, slots, n_routed, rows, S, z, xd, y, counters, out,
+                  out_shared):
+        check(lib().esp_moe_layer(xg.data_ptr(), xu.data_ptr(), L.ptr[0].data_ptr(), L.ptr[1].data_ptr(),
+                                  L.ptr[2].data_ptr(), L.k2[0].data_ptr(), L.k2[1].data_ptr(), L.k2[2].data_ptr(),
+                                  L.cb[0].data_ptr(), L.cb[1].data_ptr(), L.cb[2].data_ptr(), L.k2_host_all.data_ptr(),
+                                  L.cb_host_all.data_ptr(), L.E, L.svh_g.data_ptr(), L.svh_u.data_ptr(),
+                                  L.suh_d.data_ptr(), L.svh_d.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
+                                  members.data_ptr(), uids.numel(), members.size(1), pick.data_ptr(), wts.data_ptr(),
+                                  slots, int(n_routed), rows, L.D, L.I, int(S), z.data_ptr(), xd.data_ptr(),
+                                  y.data_ptr(), counters.data_ptr(), out.data_ptr(), ptr(out_shared), DTYPE[out.dtype],
+                                  stream_ptr(xg.device)))
 
     @staticmethod
     def moe_down(xd, L, uids, ucount, members, pick, wts, slots, n_routed, rows, y, counters, out, out_shared):

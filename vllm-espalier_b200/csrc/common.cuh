@@ -154,6 +154,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
+// GPU-scope acquire load and release add (cross-CTA readiness counters).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Thread-block cluster: this CTA's rank, a barrier of every thread of the cluster (release / acquire, so shared
 // memory written before it is visible to the other CTAs' reads after it), and loads from another CTA's shared memory.
 __device__ __forceinline__ uint32_t cluster_rank() {

@@ -187,8 +187,8 @@ __device__ __forceinline__ float scale_at(const uint2& s, int j) {
     return __half2float(__ushort_as_half((unsigned short)((j & 1) ? (w >> 16) : (w & 0xffffu))));
 }
 
-__device__ __forceinline__ void swiglu_store(const GroupedParams& p, const Scales4& sc, int n0, int pm, float cg,
-                                             float cu, float (&gv)[4], float (&uv)[4], int lane) {
+__device__ __forceinline__ void swiglu_store(__half* xd, int N, const Scales4& sc, int n0, int pm, float cg, float cu,
+                                             float (&gv)[4], float (&uv)[4], int lane) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         gv[j] *= cg;
@@ -210,7 +210,7 @@ __device__ __forceinline__ void swiglu_store(const GroupedParams& p, const Scale
     uint2 uo;
     uo.x = *reinterpret_cast<const uint32_t*>(&a);
     uo.y = *reinterpret_cast<const uint32_t*>(&bq);
-    *reinterpret_cast<uint2*>(p.xd + (size_t)pm * p.N + n0) = uo;
+    *reinterpret_cast<uint2*>(xd + (size_t)pm * N + n0) = uo;
 }
 
 // Per work item descriptor, written into shared memory by the producer and read by the consumers.
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                 const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
                 const float4 c4 = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
                 float gv[4] = {a.x, a.y, a.z, a.w}, uv[4] = {c4.x, c4.y, c4.z, c4.w};
-                swiglu_store(p, sc, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
+                swiglu_store(p.xd, p.N, sc, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
             }
         } else {   // MODE_DOWN: y for this block; row arrivals after the last item
             const float cd = cb_step(cb0);
@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
                     su.x += c4.x; su.y += c4.y; su.z += c4.z; su.w += c4.w;
                 }
                 float gv[4] = {sg.x, sg.y, sg.z, sg.w}, uv[4] = {su.x, su.y, su.z, su.w};
-                swiglu_store(p, dsc, n0, pm, cg, cu, gv, uv, lane);
+                swiglu_store(p.xd, p.N, dsc, n0, pm, cg, cu, gv, uv, lane);
             }
             if (threadIdx.x == 0) p.counters[s_pend[pi][0]] = 0;
         } else {                        // MODE_DOWN: combine the row's slots in slot order
@@ -606,6 +606,469 @@ __global__ void __launch_bounds__(GTHREADS, 1) grouped_kernel(const __grid_const
             }
             if (lane == 0) p.counters[s_pend[pi][0]] = 0;
         }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// The fused expert layer: gate/up + SwiGLU and down + combine in one persistent launch.
+//
+// One work counter hands out every gate/up item (expert entry u, 128-column block of I, k-slice), then every down
+// item (entry u, 128-column block of D), both from the last entry down. A down item's producers wait (bounded, acquire)
+// until its entry's gate/up blocks have all been finished (ready[u] == I / 128) before copying its xd slices. A
+// finisher warp takes the arrivals off the consumers: the last of a block's S slices to arrive adds the slices in
+// order and runs the SwiGLU into xd, then releases ready[u]; the last of a row's slots to finish a down block combines
+// the row in slot order. No deadlock: a waiting producer waits only for items handed out before its own, which CTAs
+// already hold and finish without waiting on anything later. Sums and orders are those of the two-launch path, so the
+// outputs are the same bits.
+// ------------------------------------------------------------------------------------------------------------------
+struct LayerParams {
+    const int* uids;
+    const int* ucount;
+    const int* members;            // [maxu][maxm] row * 32 + slot, -1 padded
+    int maxm, maxu, slots, rows, E, n_routed;
+    // gate / up: D -> I (rotated inputs xg / xu [P][D])
+    const int64_t* tp[3];          // trellis pointer tables: gate, up, down [E]
+    const int* k2[3];
+    const int* cb[3];
+    const __half* xg;
+    const __half* xu;
+    int D, I, S;
+    const __half* svh_g;
+    const __half* svh_u;
+    const __half* suh_d;
+    float* Z;                      // [2][S][P][I] slice partials (S > 1)
+    __half* xd;                    // [P][I]
+    // down: I -> D
+    const __half* svh_d;
+    const int* pick;               // [P]
+    const float* wts;              // [P]
+    float* y;                      // [P][D]
+    void* out;
+    void* out_shared;
+    int out_dtype;
+    // counters, zero on entry and left zero: slice arrivals [maxu][I/128], row arrivals [rows][D/128], the work
+    // counter, entry readiness [maxu], CTA exits
+    int* cnt_gu;
+    int* cnt_d;
+    int* work;
+    int* ready;
+    int* exits;
+};
+
+struct FinEntry {
+    int kind, u, b;                // kind 0: gate/up block (u, b) stored; 1: down block (u, b) stored; 2: no more
+};
+constexpr int FQ = 64;                             // finisher queue entries
+constexpr int LWARPS = GWARPS + GPROD + 1;         // + the finisher warp
+constexpr int LTHREADS = LWARPS * 32;
+
+__device__ __forceinline__ bool wait_ready(const int* ready, int need) {
+    if (ld_acquire_gpu(ready) >= need) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        for (int i = 0; i < 32; ++i) {
+            __nanosleep(64);
+            if (ld_acquire_gpu(ready) >= need) return true;
+        }
+        const uint64_t dt = global_ns() - t0;
+        if (dt > WAIT_NS) break;
+        if (dt > 20000 && *reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
+    }
+    report(ESP_ERR_TIMEOUT);
+    return false;
+}
+
+// Spin on a shared-memory word until it passes `v` (bounded by time like the mbarrier waits).
+__device__ __forceinline__ bool wait_smem_gt(const volatile int* w, int v) {
+    if (*w > v) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i) {
+            __nanosleep(32);
+            if (*w > v) return true;
+        }
+        const uint64_t dt = global_ns() - t0;
+        if (dt > WAIT_NS) break;
+        if (dt > 20000 && *reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
+    }
+    report(ESP_ERR_TIMEOUT);
+    return false;
+}
+
+template <int NTG, int KCAP>
+__global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constant__ LayerParams p) {
+    constexpr int GSTAGES = gstages(NTG, KCAP);
+    static_assert(GSTAGES >= 2 && GSTAGES + 2 <= NDESC, "stage ring / descriptor ring");
+    constexpr int MP = 8 * NTG;
+    constexpr int UNIT_WMAX = 8 * 8 * KCAP;
+    constexpr int SLICE_W = MP * 8;
+    constexpr int STAGE_W = GUPS * (UNIT_WMAX + SLICE_W);
+    extern __shared__ __align__(128) uint32_t smem[];
+    float* red = reinterpret_cast<float*>(smem + (size_t)GSTAGES * STAGE_W);       // [2][MP][GRED]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * MP * GRED);
+    uint64_t* empty = full + GSTAGES;
+    __shared__ ItemDesc desc[NDESC];
+    __shared__ int s_item[NDESC];
+    __shared__ FinEntry s_q[FQ];
+    __shared__ int s_qtail, s_qhead;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NBg = p.I / 128, NBd = p.D / 128;
+    const int KTg = p.D / 16, KTd = p.I / 16;
+    const int P = p.rows * p.slots;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nu = p.ucount[0];
+    const int n_gu = nu * NBg * p.S, n_items = n_gu + nu * NBd;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < GSTAGES; ++i) {
+            mbar_init(&full[i], 32 * GPROD + 1);
+            mbar_init(&empty[i], GWARPS);
+        }
+        s_qtail = 0;
+        s_qhead = 0;
+        fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < NDESC * (int)(sizeof(ItemDesc) / 4); i += LTHREADS)
+        reinterpret_cast<int*>(desc)[i] = 0;
+    __syncthreads();
+    if (blockIdx.x == 0 && warp < GWARPS) {   // rows without a valid slot get zeros
+        for (int r = warp; r < p.rows; r += GWARPS) {
+            bool any = false;
+            for (int j = 0; j < p.slots; ++j) {
+                const int e2 = p.pick[r * p.slots + j];
+                any |= e2 >= 0 && e2 < p.E;
+            }
+            if (any) continue;
+            const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int n0 = 4 * lane; n0 < p.D; n0 += 128) {
+                store4(p.out, p.out_dtype, (size_t)r * p.D + n0, zero);
+                if (p.out_shared) store4(p.out_shared, p.out_dtype, (size_t)r * p.D + n0, zero);
+            }
+        }
+    }
+
+    if (warp >= GWARPS && warp < GWARPS + GPROD) {   // ---------------- producers ----------------
+        const int pw = warp - GWARPS;
+        const uint32_t sbase = smem_addr(smem);
+        int slot = 0, phase = 0, nstage = 0, di = 0;
+        for (;; di = (di + 1) % NDESC) {
+            if (pw == 0 && lane == 0) {
+                int t = atomicAdd(p.work, 1);
+                if (t == n_items + (int)gridDim.x - 1) *p.work = 0;          // the last fetch of the launch
+                s_item[di] = t < n_items ? t : -1;
+            }
+            named_sync(2, 32 * GPROD);
+            const int t = s_item[di];
+            if (t < 0) {   // an empty stage tells the consumers there is nothing more
+                if (pw == 0) {
+                    if (lane == 0) {
+                        desc[di].it = -1;
+                        desc[di].nkt = 0;
+                        desc[di].nmats = 0;
+                        desc[di].nm = 0;
+                    }
+                    __syncwarp();
+                }
+                if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
+                cp_async_arrive(&full[slot]);
+                if (pw == 0 && lane == 0) mbar_arrive(&full[slot]);
+                break;
+            }
+            const bool down = t >= n_gu;
+            int u, b, split;
+            if (!down) {
+                const int it = n_gu - 1 - t;
+                u = it / (NBg * p.S);
+                const int r = it - u * NBg * p.S;
+                b = r / p.S;
+                split = r - b * p.S;
+            } else {
+                const int it = n_items - 1 - t;
+                u = it / NBd;
+                b = it - u * NBd;
+                split = 0;
+            }
+            const int e = p.uids[u];
+            const int code = lane < p.maxm ? p.members[u * p.maxm + lane] : -1;
+            const int row = code >= 0 ? (code >> 5) * p.slots + (code & 31) : -1;
+            const int nm = __popc(__ballot_sync(0xffffffffu, row >= 0));
+            const int K = down ? p.I : p.D, N = down ? p.D : p.I, KT = down ? KTd : KTg;
+            const int S = down ? 1 : p.S;
+            const int nmats = down ? 1 : 2;
+            const int kt0 = split * KT / S, nkt = (split + 1) * KT / S - kt0;
+            const int ta = down ? 2 : 0, tb = down ? 2 : 1;
+            if (pw == 0) {
+                ItemDesc& d = desc[di];
+                d.rows[lane] = row;
+                if (lane == 0) {
+                    d.it = t; d.e = e; d.b = b; d.split = split; d.mat0 = down; d.nmats = nmats; d.kt0 = kt0;
+                    d.nkt = nkt; d.nm = nm; d.cb0 = p.cb[ta][e]; d.K0 = p.k2[ta][e] / 2; d.cb1 = p.cb[tb][e];
+                    d.K1 = p.k2[tb][e] / 2;
+                }
+                __syncwarp();
+            }
+            if (down) {   // the entry's xd rows must be complete (every gate/up block's SwiGLU done)
+                if (lane == 0 && !wait_ready(p.ready + u, NBg)) {
+                    // gave up (status recorded): the item runs on whatever xd holds
+                }
+                __syncwarp();
+            }
+            const int n = nmats * nkt;
+            const int m = nmats == 2 ? pw : 0;
+            const int tsel = down ? 2 : m;
+            const int kstep = nmats == 2 ? 1 : 2;
+            const int ktA = kt0 + (nmats == 2 ? 0 : pw);
+            const int Km = p.k2[tsel][e] / 2;
+            const size_t kst = (size_t)(N / 16) * (8 * Km) * kstep;
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.tp[tsel][e]) +
+                                 ((size_t)ktA * (N / 16) + (size_t)b * 8) * (8 * Km) + 4 * lane;
+            const int wq = 16 * Km;
+            const __half* X = down ? p.xd : (m == 0 ? p.xg : p.xu);
+            const int r0 = __shfl_sync(0xffffffffu, row, (lane >> 1) & 31);
+            const int r1 = __shfl_sync(0xffffffffu, row, ((lane + 32) >> 1) & 31);
+            const bool x0v = lane < 2 * nm, x1v = lane + 32 < 2 * nm;
+            const __half* xp0 = X + (x0v ? (size_t)r0 * K + ktA * 16 + (lane & 1) * 8 : 0);
+            const __half* xp1 = X + (x1v ? (size_t)r1 * K + ktA * 16 + (lane & 1) * 8 : 0);
+            const uint32_t xd0 = 4 * (GUPS * UNIT_WMAX + ((lane & 1) * MP + (lane >> 1)) * 4);
+            const uint32_t xd1 = xd0 + 16 * 16;
+            for (int i0 = 0; i0 < n; i0 += GUPS) {
+                if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
+                const uint32_t sb = sbase + (uint32_t)slot * (STAGE_W * 4);
+                const int m0 = min(GUPS, n - i0);
+                for (int j = pw; j < m0; j += 2) {
+                    const uint32_t du = sb + j * (UNIT_WMAX * 4) + 16 * lane;
+                    for (int q = 0; q < wq - lane; q += 32) cp_async16_sa(du + 16 * q, wp + 4 * q);
+                    if (x0v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd0, xp0);
+                    if (x1v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd1, xp1);
+                    wp += kst;
+                    xp0 += 16 * kstep;
+                    xp1 += 16 * kstep;
+                }
+                cp_async_arrive(&full[slot]);
+                if (pw == 0 && lane == 0) mbar_arrive(&full[slot]);
+                ++nstage;
+                if (++slot == GSTAGES) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        return;
+    }
+
+    if (warp == GWARPS + GPROD) {   // ---------------- finisher ----------------
+        int head = 0;
+        for (;;) {
+            if (!wait_smem_gt(&s_qtail, head)) break;
+            __threadfence_block();
+            const FinEntry f = s_q[head % FQ];
+            if (f.kind == 2) break;
+            const int e = p.uids[f.u];
+            const int n0 = f.b * 128 + 4 * lane;
+            if (f.kind == 0) {   // a gate/up block's slice: the last of the S adds them and runs the SwiGLU
+                int last = 0;
+                if (lane == 0) last = arrive_acq_rel(&p.cnt_gu[f.u * NBg + f.b]) == p.S - 1;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    const float cg = cb_step(p.cb[0][e]), cu = cb_step(p.cb[1][e]);
+                    const Scales4 sc{ld_scales4(p.svh_g, e, p.I, n0), ld_scales4(p.svh_u, e, p.I, n0),
+                                     ld_scales4(p.suh_d, e, p.I, n0)};
+                    for (int m = 0; m < p.maxm; ++m) {
+                        const int code = p.members[f.u * p.maxm + m];
+                        if (code < 0) break;
+                        const int pm = (code >> 5) * p.slots + (code & 31);
+                        float4 sg = make_float4(0.f, 0.f, 0.f, 0.f), su = sg;
+                        for (int s2 = 0; s2 < p.S; ++s2) {
+                            const float4 a = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)s2 * P + pm) * p.I + n0));
+                            const float4 c4 =
+                                __ldcg(reinterpret_cast<const float4*>(p.Z + (((size_t)p.S + s2) * P + pm) * p.I + n0));
+                            sg.x += a.x; sg.y += a.y; sg.z += a.z; sg.w += a.w;
+                            su.x += c4.x; su.y += c4.y; su.z += c4.z; su.w += c4.w;
+                        }
+                        float gv[4] = {sg.x, sg.y, sg.z, sg.w}, uv[4] = {su.x, su.y, su.z, su.w};
+                        swiglu_store(p.xd, p.I, sc, n0, pm, cg, cu, gv, uv, lane);
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        p.cnt_gu[f.u * NBg + f.b] = 0;
+                        red_release_gpu_add(p.ready + f.u, 1);
+                    }
+                }
+            } else {             // a down block of the entry's members: the last of a row's slots combines the row
+                const int code = lane < p.maxm ? p.members[f.u * p.maxm + lane] : -1;
+                int r = -1, last = 0;
+                if (code >= 0) {
+                    r = code >> 5;
+                    int target = 0;
+                    for (int j = 0; j < p.slots; ++j) {
+                        const int e2 = p.pick[r * p.slots + j];
+                        target += e2 >= 0 && e2 < p.E;
+                    }
+                    last = arrive_acq_rel(&p.cnt_d[r * NBd + f.b]) == target - 1;
+                }
+                unsigned lastm = __ballot_sync(0xffffffffu, last);
+                while (lastm) {
+                    const int src = __ffs(lastm) - 1;
+                    lastm &= lastm - 1;
+                    const int rr = __shfl_sync(0xffffffffu, r, src);
+                    float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int j = 0; j < p.n_routed; ++j) {
+                        const int q = rr * p.slots + j;
+                        const int e2 = p.pick[q];
+                        if (e2 < 0 || e2 >= p.E) continue;
+                        const float wq = p.wts[q];
+                        const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.D + n0));
+                        acc4[0] = fmaf(wq, yv.x, acc4[0]);
+                        acc4[1] = fmaf(wq, yv.y, acc4[1]);
+                        acc4[2] = fmaf(wq, yv.z, acc4[2]);
+                        acc4[3] = fmaf(wq, yv.w, acc4[3]);
+                    }
+                    store4(p.out, p.out_dtype, (size_t)rr * p.D + n0, acc4);
+                    if (p.out_shared && p.n_routed < p.slots) {
+                        const int q = rr * p.slots + p.n_routed;
+                        const int e2 = p.pick[q];
+                        float sv[4] = {0.f, 0.f, 0.f, 0.f};
+                        if (e2 >= 0 && e2 < p.E) {
+                            const float wq = p.wts[q];
+                            const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.D + n0));
+                            sv[0] = wq * yv.x; sv[1] = wq * yv.y; sv[2] = wq * yv.z; sv[3] = wq * yv.w;
+                        }
+                        store4(p.out_shared, p.out_dtype, (size_t)rr * p.D + n0, sv);
+                    }
+                    if (lane == 0) p.cnt_d[rr * NBd + f.b] = 0;
+                }
+            }
+            ++head;
+            __syncwarp();
+            if (lane == 0) *reinterpret_cast<volatile int*>(&s_qhead) = head;
+        }
+    } else {                         // ---------------- consumers ----------------
+        const int grp = warp >> 3, wl = warp & 7;
+        const int g = lane >> 2, t = lane & 3;
+        constexpr int CT = GWARPS * 32;
+        int slot = 0, phase = 0, di = 0;
+        auto enqueue = [&](int kind, int u, int b) {   // thread 0
+            const int tail = s_qtail;
+            if (!wait_smem_gt(&s_qhead, tail - FQ)) return;   // room in the queue (the finisher frees entries)
+            s_q[tail % FQ] = FinEntry{kind, u, b};
+            __threadfence_block();
+            *reinterpret_cast<volatile int*>(&s_qtail) = tail + 1;
+        };
+        for (;; di = (di + 1) % NDESC) {
+            float acc[2][NTG][4];
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2)
+#pragma unroll
+                for (int q = 0; q < NTG; ++q) acc[e2][q][0] = acc[e2][q][1] = acc[e2][q][2] = acc[e2][q][3] = 0.f;
+            const ItemDesc* d = &desc[di];
+            int nkt = 0, nmats = 0, ntg = 0, mcb = 0, mK = 0, item = -1;
+            Scales4 sc{};
+            for (int i0 = 0;; i0 += GUPS) {
+                if (!mbar_wait(&full[slot], phase)) {
+                    item = -1;
+                    break;
+                }
+                if (i0 == 0) {
+                    item = d->it;
+                    nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
+                    const bool mB = nmats == 2 && grp == 1;
+                    mcb = mB ? d->cb1 : d->cb0;
+                    mK = mB ? d->K1 : d->K0;
+                    if (item >= 0) {
+                        const int n0s = d->b * 128 + 4 * lane;
+                        if (item >= n_gu) {
+                            sc.d = ld_scales4(p.svh_d, d->e, p.D, n0s);
+                        } else if (p.S == 1) {
+                            sc.g = ld_scales4(p.svh_g, d->e, p.I, n0s);
+                            sc.u = ld_scales4(p.svh_u, d->e, p.I, n0s);
+                            sc.d = ld_scales4(p.suh_d, d->e, p.I, n0s);
+                        }
+                    }
+                }
+                const int n = nmats * nkt;
+                const uint32_t* st = smem + (size_t)slot * STAGE_W;
+                const int m0 = min(GUPS, n - i0);
+                if (m0 > 0)
+                    dispatch_units<NTG, KCAP>(mcb, mK, st, st + GUPS * UNIT_WMAX, 0, m0, UNIT_WMAX, SLICE_W, grp, wl,
+                                              lane, ntg, acc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (++slot == GSTAGES) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+                if (i0 + GUPS >= n) break;
+            }
+            if (item < 0) break;
+
+            const int col = wl * 16 + g;
+            for (int gi = 0; gi < 2; ++gi) {
+                if (gi == grp || nmats == 2) {
+                    const bool add = nmats == 1 && gi == 1;
+                    float* base = red + (size_t)(nmats == 2 ? grp : 0) * MP * GRED + col;
+#pragma unroll
+                    for (int q = 0; q < NTG; ++q) {
+                        float* rr = base + (size_t)(8 * q + 2 * t) * GRED;
+                        const float v0 = acc[0][q][0] + acc[1][q][0], v1 = acc[0][q][1] + acc[1][q][1];
+                        const float v2 = acc[0][q][2] + acc[1][q][2], v3 = acc[0][q][3] + acc[1][q][3];
+                        if (!add) {
+                            rr[0] = v0; rr[GRED] = v1; rr[8] = v2; rr[GRED + 8] = v3;
+                        } else {
+                            rr[0] += v0; rr[GRED] += v1; rr[8] += v2; rr[GRED + 8] += v3;
+                        }
+                    }
+                }
+                named_sync(1, CT);
+                if (nmats == 2) break;
+            }
+            const int cb0 = d->cb0, cb1 = d->cb1, b = d->b, nm = d->nm;
+            const bool down = item >= n_gu;
+            const int u = down ? (n_items - 1 - item) / NBd : (n_gu - 1 - item) / (NBg * p.S);
+            if (!down && p.S > 1) {            // slice partials for the finisher
+                const int n0 = b * 128 + 4 * lane;
+                for (int m = warp; m < nm; m += GWARPS)
+                    for (int mi = 0; mi < 2; ++mi)
+                        *reinterpret_cast<float4*>(p.Z + (((size_t)mi * p.S + d->split) * P + d->rows[m]) * p.I + n0) =
+                            *reinterpret_cast<const float4*>(red + ((size_t)mi * MP + m) * GRED + 4 * lane);
+                named_sync(1, CT);
+                if (threadIdx.x == 0) enqueue(0, u, b);
+            } else if (!down) {                // the whole of K in this item: the SwiGLU now, then the entry's release
+                const int n0 = b * 128 + 4 * lane;
+                for (int m = warp; m < nm; m += GWARPS) {
+                    const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                    const float4 c4 = *reinterpret_cast<const float4*>(red + ((size_t)MP + m) * GRED + 4 * lane);
+                    float gv[4] = {a.x, a.y, a.z, a.w}, uv[4] = {c4.x, c4.y, c4.z, c4.w};
+                    swiglu_store(p.xd, p.I, sc, n0, d->rows[m], cb_step(cb0), cb_step(cb1), gv, uv, lane);
+                }
+                named_sync(1, CT);
+                if (threadIdx.x == 0) red_release_gpu_add(p.ready + u, 1);
+            } else {                           // y for this block, then the rows' arrivals through the finisher
+                const float cd = cb_step(cb0);
+                const int n0 = b * 128 + 4 * lane;
+                for (int m = warp; m < nm; m += GWARPS) {
+                    const float4 a = *reinterpret_cast<const float4*>(red + (size_t)m * GRED + 4 * lane);
+                    float v[4] = {a.x * cd, a.y * cd, a.z * cd, a.w * cd};
+                    fwht128(v, lane);
+                    float4 o;
+                    o.x = v[0] * HAD_SCALE * scale_at(sc.d, 0);
+                    o.y = v[1] * HAD_SCALE * scale_at(sc.d, 1);
+                    o.z = v[2] * HAD_SCALE * scale_at(sc.d, 2);
+                    o.w = v[3] * HAD_SCALE * scale_at(sc.d, 3);
+                    *reinterpret_cast<float4*>(p.y + (size_t)d->rows[m] * p.D + n0) = o;
+                }
+                named_sync(1, CT);
+                if (threadIdx.x == 0) enqueue(1, u, b);
+            }
+            named_sync(1, CT);   // red and the descriptor are free for the next item
+        }
+        if (threadIdx.x == 0) enqueue(2, 0, 0);
+    }
+    // the last CTA to leave resets the entries' readiness (every producer of every CTA is past its waits by then)
+    named_sync(3, GWARPS * 32 + 32);
+    if (threadIdx.x == 0 && arrive_acq_rel(p.exits) == (int)gridDim.x - 1) {
+        for (int i = 0; i < p.maxu; ++i) p.ready[i] = 0;
+        *p.exits = 0;
     }
 }
 
@@ -806,6 +1269,31 @@ int launch_grouped(const GroupedParams& p, int ntg, int kmax, int maxu, void* st
 #undef ESP_G
 }
 
+template <int NTG, int KCAP>
+int launch_layer_t(const LayerParams& p, dim3 grid, void* stream) {
+    auto kern = layer_kernel<NTG, KCAP>;
+    const size_t smem = grouped_smem(NTG, KCAP);
+    static bool opted = false;
+    if (!opted) {
+        if (int rc = allow_smem(kern, smem)) return rc;
+        opted = true;
+    }
+    return launch(kern, grid, dim3(LTHREADS), smem, stream, true, p);
+}
+
+int launch_layer(const LayerParams& p, int ntg, int kmax, void* stream) {
+    const dim3 grid((unsigned)device_sms());   // persistent: one CTA an SM, items handed out dynamically
+#define ESP_L(N_) \
+    return kmax <= 4 ? launch_layer_t<N_, 4>(p, grid, stream) : launch_layer_t<N_, 8>(p, grid, stream);
+    switch (ntg) {
+        case 1: ESP_L(1)
+        case 2: ESP_L(2)
+        case 3: ESP_L(3)
+        default: ESP_L(4)
+    }
+#undef ESP_L
+}
+
 int check_tables(const int* k2_host, const int* cb_host, int E, int& kmax) {
     kmax = 0;
     for (int e = 0; e < E; ++e) {
@@ -933,6 +1421,59 @@ int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const
     p.n_routed = n_routed;
     if (int rc = launch_grouped(p, (maxm + 7) / 8, kmax, maxu, stream)) return rc;
     return ok();
+}
+
+// The fused expert layer in one launch: gate/up + SwiGLU and down + combine (the sequence of esp_moe_gateup and
+// esp_moe_down, the same output bits).
+int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u, const int64_t* tp_d,
+                  const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g, const int* cb_u, const int* cb_d,
+                  const int* k2_host, const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u,
+                  const uint16_t* suh_d, const uint16_t* svh_d, const int* uids, const int* ucount, const int* members,
+                  int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed, int rows, int D, int I,
+                  int S, float* Z, uint16_t* xd, float* y, int* counters, void* out, void* out_shared, int out_dtype,
+                  void* stream) {
+    ESP_REQUIRE(xg && xu && tp_g && tp_u && tp_d && k2_g && k2_u && k2_d && cb_g && cb_u && cb_d && k2_host &&
+                    cb_host && svh_g && svh_u && suh_d && svh_d && uids && ucount && members && pick && wts && xd &&
+                    y && counters && out,
+                ESP_ERR_INVALID, "moe_layer: null pointer");
+    ESP_REQUIRE(D % 128 == 0 && I % 128 == 0 && S >= 1 && D / 16 >= S && D / 128 <= 256, ESP_ERR_INVALID,
+                "moe_layer: shapes");
+    ESP_REQUIRE(S == 1 || Z, ESP_ERR_SCRATCH, "moe_layer: split partials need Z");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && slots >= 1 && slots <= 32 && n_routed <= slots && rows >= 0,
+                ESP_ERR_INVALID, "moe_layer: limits (32 members, 32 slots)");
+    ESP_REQUIRE(out_dtype >= 0 && out_dtype <= 2, ESP_ERR_INVALID, "moe_layer: dtype");
+    int km = 0, kmax = 0;
+    for (int t = 0; t < 3; ++t) {
+        if (int rc = check_tables(k2_host + t * E, cb_host + t * E, E, km)) return rc;
+        kmax = std::max(kmax, km);
+    }
+    LayerParams p = {};
+    p.uids = uids; p.ucount = ucount; p.members = members;
+    p.maxm = maxm; p.maxu = maxu; p.slots = slots; p.rows = rows; p.E = E; p.n_routed = n_routed;
+    p.tp[0] = tp_g; p.tp[1] = tp_u; p.tp[2] = tp_d;
+    p.k2[0] = k2_g; p.k2[1] = k2_u; p.k2[2] = k2_d;
+    p.cb[0] = cb_g; p.cb[1] = cb_u; p.cb[2] = cb_d;
+    p.xg = reinterpret_cast<const __half*>(xg);
+    p.xu = reinterpret_cast<const __half*>(xu);
+    p.D = D; p.I = I; p.S = S;
+    p.svh_g = reinterpret_cast<const __half*>(svh_g);
+    p.svh_u = reinterpret_cast<const __half*>(svh_u);
+    p.suh_d = reinterpret_cast<const __half*>(suh_d);
+    p.Z = Z;
+    p.xd = reinterpret_cast<__half*>(xd);
+    p.svh_d = reinterpret_cast<const __half*>(svh_d);
+    p.pick = pick; p.wts = wts; p.y = y; p.out = out; p.out_shared = out_shared; p.out_dtype = out_dtype;
+    p.cnt_gu = counters;
+    p.cnt_d = p.cnt_gu + (size_t)maxu * (I / 128);
+    p.work = p.cnt_d + (size_t)rows * (D / 128);
+    p.ready = p.work + 1;
+    p.exits = p.ready + maxu;
+    if (int rc = launch_layer(p, (maxm + 7) / 8, kmax, stream)) return rc;
+    return ok();
+}
+
+size_t esp_moe_layer_counters(int maxu, int rows, int D, int I) {
+    return (size_t)maxu * (I / 128) + (size_t)rows * (D / 128) + 2 + (size_t)maxu;
 }
 
 int esp_gateup_epilogue(const float* Z, const int* pick, const uint16_t* svh_g, const uint16_t* svh_u,

@@ -24,6 +24,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from ._env import MOE_ONE_LAUNCH
 from ._lib import ext, lib  # noqa: F401  (ext is part of this module's reference surface)
 
 # Espalier grid code (EspMatrix.cb) -> the kernels' codebook id (1 mcg, 3 E2M1, 6 int5, 7 int6)
@@ -80,6 +81,19 @@ class Layer:
     cb_host_gu: torch.Tensor | None = None
     k2_host_d: torch.Tensor | None = None
     cb_host_d: torch.Tensor | None = None
+
+    @property
+    def k2_host_all(self) -> torch.Tensor:
+        """[3][E] gate, up, down (the one-launch layer's host tables), built once and kept: the C call reads it."""
+        if "_k2_all" not in self.__dict__:
+            self.__dict__["_k2_all"] = torch.cat([self.k2_host_gu.reshape(-1), self.k2_host_d.reshape(-1)]).contiguous()
+        return self.__dict__["_k2_all"]
+
+    @property
+    def cb_host_all(self) -> torch.Tensor:
+        if "_cb_all" not in self.__dict__:
+            self.__dict__["_cb_all"] = torch.cat([self.cb_host_gu.reshape(-1), self.cb_host_d.reshape(-1)]).contiguous()
+        return self.__dict__["_cb_all"]
 
 
 def prepare(experts, shared=None, gate_w=None) -> Layer:
@@ -157,6 +171,9 @@ class Scratch:
         # gate/up slice arrivals and per-row slot arrivals, each followed by the launch's work-item counter
         self.cnt_gu = torch.zeros((maxu * (I // 128) + 1,), dtype=torch.int32, device=device)
         self.cnt_d = torch.zeros((rows * (D // 128) + 1,), dtype=torch.int32, device=device)
+        # the one-launch layer's counters: slice arrivals, row arrivals, work, readiness, exits
+        self.cnt_layer = torch.zeros((int(lib().esp_moe_layer_counters(maxu, rows, D, I)),), dtype=torch.int32,
+                                     device=device)
         self.rows, self.slots, self.E = rows, slots, E
 
     def window(self, R: int):
@@ -245,13 +262,17 @@ def routed2(x: torch.Tensor, pick: torch.Tensor | None, wts: torch.Tensor | None
     if pick is not None:
         e.group_shared(pick, wts, x, x.stride(0), L.gate_w, L.shared_id, pk, wt, ids, s.count, members, R, k, E)
     e.rot_in(x, x.stride(0), pk, L.suh_g, L.suh_u, s.xg, s.xu, R, D, slots, E)
-    e.moe_gateup(s.xg, s.xu, L, ids, s.count, members, slots, P, s.S, s.z, s.cnt_gu, s.xd)
     if out is None:
         out = torch.empty((R, D), dtype=x.dtype, device=x.device)
     if L.shared_id >= 0 and out_shared is None:
         out_shared = torch.empty((R, D), dtype=x.dtype, device=x.device)
-    e.moe_down(s.xd, L, ids, s.count, members, pk, wt, slots, k, R, s.y, s.cnt_d, out,
-               out_shared if L.shared_id >= 0 else None)
+    if MOE_ONE_LAUNCH:
+        e.moe_layer(s.xg, s.xu, L, ids, s.count, members, pk, wt, slots, k, R, s.S, s.z, s.xd, s.y, s.cnt_layer, out,
+                    out_shared if L.shared_id >= 0 else None)
+    else:
+        e.moe_gateup(s.xg, s.xu, L, ids, s.count, members, slots, P, s.S, s.z, s.cnt_gu, s.xd)
+        e.moe_down(s.xd, L, ids, s.count, members, pk, wt, slots, k, R, s.y, s.cnt_d, out,
+                   out_shared if L.shared_id >= 0 else None)
     return out, (out_shared if L.shared_id >= 0 else None)
 
 
