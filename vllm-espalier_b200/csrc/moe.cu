@@ -143,17 +143,33 @@ __device__ __forceinline__ void stage_units(const uint32_t* st, const uint32_t* 
     constexpr int TW = 8 * K;
     // this group's units are every other one; consecutive ones alternate between two accumulator sets (static indices,
     // so the accumulators stay in registers)
-    auto unit = [&](int jj, float (&ac)[NTG][4]) {
-        uint32_t a[4];
-        decode_a<CB, K>(st + jj * unit_w + wl * TW, lane, a);
+    auto mmas = [&](int jj, const uint32_t (&a)[4], float (&ac)[NTG][4]) {
         const uint32_t* xs = xs0 + jj * slice_w;
 #pragma unroll
         for (int q = 0; q < NTG; ++q)
             if (q < ntg) mma16816(ac[q], a, xs[(8 * q + g) * 4 + t], xs[(8 * NTG + 8 * q + g) * 4 + t]);
     };
+    // two units decoded back to back before their MMAs: no branch between the two decode chains, so they interleave
+    auto pair = [&](int ja, int jb) {
+        uint32_t a[4], b[4];
+        decode_a<CB, K>(st + ja * unit_w + wl * TW, lane, a);
+        decode_a<CB, K>(st + jb * unit_w + wl * TW, lane, b);
+        mmas(ja, a, acc[0]);
+        mmas(jb, b, acc[1]);
+    };
+    if (j0 == 0 && j1 == GUPS) {   // a whole stage (the common case): straight-line code
+#pragma unroll
+        for (int j2 = 0; j2 < GUPS; j2 += 4) pair(j2 + grp, j2 + grp + 2);
+        return;
+    }
     for (int jj = j0 + ((j0 & 1) != grp ? 1 : 0); jj < j1; jj += 4) {
-        unit(jj, acc[0]);
-        if (jj + 2 < j1) unit(jj + 2, acc[1]);
+        if (jj + 2 < j1) {
+            pair(jj, jj + 2);
+        } else {
+            uint32_t a[4];
+            decode_a<CB, K>(st + jj * unit_w + wl * TW, lane, a);
+            mmas(jj, a, acc[0]);
+        }
     }
 }
 
@@ -657,8 +673,11 @@ struct LayerParams {
 
 struct FinEntry {
     int kind, u, b;                // kind 0: gate/up block (u, b) stored; 1: down block (u, b) stored; 2: no more
+    int e, nm;                     // the entry's expert and member count
+    float c0, c1;                  // codebook steps (gate, up)
 };
-constexpr int FQ = 64;                             // finisher queue entries
+constexpr int FQ = 32;                             // finisher queue entries
+constexpr int LMAXP = 32 * 32;                     // slots a call (32 rows x 32 slots at most)
 constexpr int LWARPS = GWARPS + GPROD + 1;         // + the finisher warp
 constexpr int LTHREADS = LWARPS * 32;
 
@@ -710,7 +729,11 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
     __shared__ ItemDesc desc[NDESC];
     __shared__ int s_item[NDESC];
     __shared__ FinEntry s_q[FQ];
+    __shared__ int s_qrows[FQ][32];                // each queued item's member slots (row * slots + slot)
     __shared__ int s_qtail, s_qhead;
+    __shared__ float s_w[LMAXP];                   // the finisher's copies of the call's weights,
+    __shared__ unsigned char s_ok[LMAXP];          // which slots are valid,
+    __shared__ int s_tgt[32];                      // and each row's valid slot count
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NBg = p.I / 128, NBd = p.D / 128;
@@ -752,10 +775,19 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
         const int pw = warp - GWARPS;
         const uint32_t sbase = smem_addr(smem);
         int slot = 0, phase = 0, nstage = 0, di = 0;
+        bool first = true;
         for (;; di = (di + 1) % NDESC) {
             if (pw == 0 && lane == 0) {
-                int t = atomicAdd(p.work, 1);
-                if (t == n_items + (int)gridDim.x - 1) *p.work = 0;          // the last fetch of the launch
+                // a CTA's first item is its own index (no atomic on the critical path); the rest come from the
+                // counter, offset by the grid. Every CTA with a first item makes exactly one failing fetch, so the
+                // fetches number n_items and the one that returns n_items - 1 is the launch's last: it resets.
+                int t = blockIdx.x;
+                if (!first) {
+                    const int c = atomicAdd(p.work, 1);
+                    if (c == n_items - 1) *p.work = 0;
+                    t = c + (int)gridDim.x;
+                }
+                first = false;
                 s_item[di] = t < n_items ? t : -1;
             }
             named_sync(2, 32 * GPROD);
@@ -808,12 +840,6 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
                 }
                 __syncwarp();
             }
-            if (down) {   // the entry's xd rows must be complete (every gate/up block's SwiGLU done)
-                if (lane == 0 && !wait_ready(p.ready + u, NBg)) {
-                    // gave up (status recorded): the item runs on whatever xd holds
-                }
-                __syncwarp();
-            }
             const int n = nmats * nkt;
             const int m = nmats == 2 ? pw : 0;
             const int tsel = down ? 2 : m;
@@ -832,7 +858,45 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
             const __half* xp1 = X + (x1v ? (size_t)r1 * K + ktA * 16 + (lane & 1) * 8 : 0);
             const uint32_t xd0 = 4 * (GUPS * UNIT_WMAX + ((lane & 1) * MP + (lane >> 1)) * 4);
             const uint32_t xd1 = xd0 + 16 * 16;
-            for (int i0 = 0; i0 < n; i0 += GUPS) {
+            int i0 = 0;
+            if (down) {
+                // the weights do not depend on the gate/up results: the first stages (as many as the ring holds) get
+                // theirs before the entry's readiness wait (every gate/up block's SwiGLU done), their xd slices after
+                int ps = slot;
+                for (int npf = 0; i0 < n && npf < GSTAGES; i0 += GUPS, ++npf) {
+                    if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
+                    const uint32_t sb = sbase + (uint32_t)slot * (STAGE_W * 4);
+                    const int m0 = min(GUPS, n - i0);
+                    for (int j = pw; j < m0; j += 2) {
+                        const uint32_t du = sb + j * (UNIT_WMAX * 4) + 16 * lane;
+                        for (int q = 0; q < wq - lane; q += 32) cp_async16_sa(du + 16 * q, wp + 4 * q);
+                        wp += kst;
+                    }
+                    ++nstage;
+                    if (++slot == GSTAGES) {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (lane == 0 && !wait_ready(p.ready + u, NBg)) {
+                    // gave up (status recorded): the item runs on whatever xd holds
+                }
+                __syncwarp();
+                for (int i1 = 0; i1 < i0; i1 += GUPS) {
+                    const uint32_t sb = sbase + (uint32_t)ps * (STAGE_W * 4);
+                    const int m0 = min(GUPS, n - i1);
+                    for (int j = pw; j < m0; j += 2) {
+                        if (x0v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd0, xp0);
+                        if (x1v) cp_async16_sa(sb + j * (SLICE_W * 4) + xd1, xp1);
+                        xp0 += 16 * kstep;
+                        xp1 += 16 * kstep;
+                    }
+                    cp_async_arrive(&full[ps]);
+                    if (pw == 0 && lane == 0) mbar_arrive(&full[ps]);
+                    if (++ps == GSTAGES) ps = 0;
+                }
+            }
+            for (; i0 < n; i0 += GUPS) {
                 if (nstage >= GSTAGES && !mbar_wait(&empty[slot], phase ^ 1)) return;
                 const uint32_t sb = sbase + (uint32_t)slot * (STAGE_W * 4);
                 const int m0 = min(GUPS, n - i0);
@@ -858,36 +922,57 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
     }
 
     if (warp == GWARPS + GPROD) {   // ---------------- finisher ----------------
+        // everything but the arrivals and the partial sums comes from shared memory: the queue entry (expert, steps,
+        // member slots) and the call's picks / weights / per-row counts, loaded here while the first items decode
+        for (int q = lane; q < P; q += 32) {
+            const int e2 = p.pick[q];
+            s_ok[q] = e2 >= 0 && e2 < p.E;
+            s_w[q] = p.wts[q];
+        }
+        __syncwarp();
+        for (int r = lane; r < p.rows; r += 32) {
+            int c = 0;
+            for (int j = 0; j < p.slots; ++j) c += s_ok[r * p.slots + j];
+            s_tgt[r] = c;
+        }
+        __syncwarp();
         int head = 0;
         for (;;) {
             if (!wait_smem_gt(&s_qtail, head)) break;
             __threadfence_block();
             const FinEntry f = s_q[head % FQ];
+            const int* qrows = s_qrows[head % FQ];
             if (f.kind == 2) break;
-            const int e = p.uids[f.u];
             const int n0 = f.b * 128 + 4 * lane;
             if (f.kind == 0) {   // a gate/up block's slice: the last of the S adds them and runs the SwiGLU
+                const Scales4 sc{ld_scales4(p.svh_g, f.e, p.I, n0), ld_scales4(p.svh_u, f.e, p.I, n0),
+                                 ld_scales4(p.suh_d, f.e, p.I, n0)};   // constant data: loaded ahead of the arrival
                 int last = 0;
                 if (lane == 0) last = arrive_acq_rel(&p.cnt_gu[f.u * NBg + f.b]) == p.S - 1;
                 last = __shfl_sync(0xffffffffu, last, 0);
+                __syncwarp();
                 if (last) {
-                    const float cg = cb_step(p.cb[0][e]), cu = cb_step(p.cb[1][e]);
-                    const Scales4 sc{ld_scales4(p.svh_g, e, p.I, n0), ld_scales4(p.svh_u, e, p.I, n0),
-                                     ld_scales4(p.suh_d, e, p.I, n0)};
-                    for (int m = 0; m < p.maxm; ++m) {
-                        const int code = p.members[f.u * p.maxm + m];
-                        if (code < 0) break;
-                        const int pm = (code >> 5) * p.slots + (code & 31);
+                    for (int m = 0; m < f.nm; ++m) {
+                        const int pm = qrows[m];
                         float4 sg = make_float4(0.f, 0.f, 0.f, 0.f), su = sg;
-                        for (int s2 = 0; s2 < p.S; ++s2) {
-                            const float4 a = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)s2 * P + pm) * p.I + n0));
-                            const float4 c4 =
-                                __ldcg(reinterpret_cast<const float4*>(p.Z + (((size_t)p.S + s2) * P + pm) * p.I + n0));
-                            sg.x += a.x; sg.y += a.y; sg.z += a.z; sg.w += a.w;
-                            su.x += c4.x; su.y += c4.y; su.z += c4.z; su.w += c4.w;
+                        for (int s0 = 0; s0 < p.S; s0 += 2) {   // two slices' loads in flight, added in order
+                            float4 a[2], c4[2];
+#pragma unroll
+                            for (int q = 0; q < 2; ++q)
+                                if (s0 + q < p.S) {
+                                    a[q] = __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)(s0 + q) * P + pm) * p.I + n0));
+                                    c4[q] = __ldcg(reinterpret_cast<const float4*>(
+                                        p.Z + (((size_t)p.S + s0 + q) * P + pm) * p.I + n0));
+                                }
+#pragma unroll
+                            for (int q = 0; q < 2; ++q)
+                                if (s0 + q < p.S) {
+                                    sg.x += a[q].x; sg.y += a[q].y; sg.z += a[q].z; sg.w += a[q].w;
+                                    su.x += c4[q].x; su.y += c4[q].y; su.z += c4[q].z; su.w += c4[q].w;
+                                }
                         }
                         float gv[4] = {sg.x, sg.y, sg.z, sg.w}, uv[4] = {su.x, su.y, su.z, su.w};
-                        swiglu_store(p.xd, p.I, sc, n0, pm, cg, cu, gv, uv, lane);
+                        swiglu_store(p.xd, p.I, sc, n0, pm, f.c0, f.c1, gv, uv, lane);
                     }
                     __syncwarp();
                     if (lane == 0) {
@@ -896,43 +981,44 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
                     }
                 }
             } else {             // a down block of the entry's members: the last of a row's slots combines the row
-                const int code = lane < p.maxm ? p.members[f.u * p.maxm + lane] : -1;
                 int r = -1, last = 0;
-                if (code >= 0) {
-                    r = code >> 5;
-                    int target = 0;
-                    for (int j = 0; j < p.slots; ++j) {
-                        const int e2 = p.pick[r * p.slots + j];
-                        target += e2 >= 0 && e2 < p.E;
-                    }
-                    last = arrive_acq_rel(&p.cnt_d[r * NBd + f.b]) == target - 1;
+                if (lane < f.nm) {
+                    r = qrows[lane] / p.slots;
+                    last = arrive_acq_rel(&p.cnt_d[r * NBd + f.b]) == s_tgt[r] - 1;
                 }
                 unsigned lastm = __ballot_sync(0xffffffffu, last);
+                __syncwarp();
                 while (lastm) {
                     const int src = __ffs(lastm) - 1;
                     lastm &= lastm - 1;
                     const int rr = __shfl_sync(0xffffffffu, r, src);
+                    const int q0 = rr * p.slots;
+                    const bool shs = p.out_shared && p.n_routed < p.slots && s_ok[q0 + p.n_routed];
+                    float4 ysh = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (shs) ysh = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)(q0 + p.n_routed) * p.D + n0));
                     float acc4[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int j = 0; j < p.n_routed; ++j) {
-                        const int q = rr * p.slots + j;
-                        const int e2 = p.pick[q];
-                        if (e2 < 0 || e2 >= p.E) continue;
-                        const float wq = p.wts[q];
-                        const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.D + n0));
-                        acc4[0] = fmaf(wq, yv.x, acc4[0]);
-                        acc4[1] = fmaf(wq, yv.y, acc4[1]);
-                        acc4[2] = fmaf(wq, yv.z, acc4[2]);
-                        acc4[3] = fmaf(wq, yv.w, acc4[3]);
+                    for (int j0 = 0; j0 < p.n_routed; j0 += 8) {   // eight slots' loads in flight, summed in order
+                        float4 yv[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            if (j0 + q < p.n_routed && s_ok[q0 + j0 + q])
+                                yv[q] = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)(q0 + j0 + q) * p.D + n0));
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            if (j0 + q < p.n_routed && s_ok[q0 + j0 + q]) {
+                                const float wq = s_w[q0 + j0 + q];
+                                acc4[0] = fmaf(wq, yv[q].x, acc4[0]);
+                                acc4[1] = fmaf(wq, yv[q].y, acc4[1]);
+                                acc4[2] = fmaf(wq, yv[q].z, acc4[2]);
+                                acc4[3] = fmaf(wq, yv[q].w, acc4[3]);
+                            }
                     }
                     store4(p.out, p.out_dtype, (size_t)rr * p.D + n0, acc4);
                     if (p.out_shared && p.n_routed < p.slots) {
-                        const int q = rr * p.slots + p.n_routed;
-                        const int e2 = p.pick[q];
                         float sv[4] = {0.f, 0.f, 0.f, 0.f};
-                        if (e2 >= 0 && e2 < p.E) {
-                            const float wq = p.wts[q];
-                            const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.D + n0));
-                            sv[0] = wq * yv.x; sv[1] = wq * yv.y; sv[2] = wq * yv.z; sv[3] = wq * yv.w;
+                        if (shs) {
+                            const float wq = s_w[q0 + p.n_routed];
+                            sv[0] = wq * ysh.x; sv[1] = wq * ysh.y; sv[2] = wq * ysh.z; sv[3] = wq * ysh.w;
                         }
                         store4(p.out_shared, p.out_dtype, (size_t)rr * p.D + n0, sv);
                     }
@@ -948,12 +1034,20 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
         const int g = lane >> 2, t = lane & 3;
         constexpr int CT = GWARPS * 32;
         int slot = 0, phase = 0, di = 0;
-        auto enqueue = [&](int kind, int u, int b) {   // thread 0
-            const int tail = s_qtail;
-            if (!wait_smem_gt(&s_qhead, tail - FQ)) return;   // room in the queue (the finisher frees entries)
-            s_q[tail % FQ] = FinEntry{kind, u, b};
-            __threadfence_block();
-            *reinterpret_cast<volatile int*>(&s_qtail) = tail + 1;
+        auto enqueue = [&](int kind, int u, const ItemDesc* d) {   // warp 0
+            const int tail = *reinterpret_cast<volatile int*>(&s_qtail);
+            int room = 1;
+            if (lane == 0) room = wait_smem_gt(&s_qhead, tail - FQ);   // the finisher frees entries
+            if (!__shfl_sync(0xffffffffu, room, 0)) return;
+            if (d) s_qrows[tail % FQ][lane] = d->rows[lane];
+            if (lane == 0)
+                s_q[tail % FQ] = d ? FinEntry{kind, u, d->b, d->e, d->nm, cb_step(d->cb0), cb_step(d->cb1)}
+                                   : FinEntry{kind, 0, 0, 0, 0, 0.f, 0.f};
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                *reinterpret_cast<volatile int*>(&s_qtail) = tail + 1;
+            }
         };
         for (;; di = (di + 1) % NDESC) {
             float acc[2][NTG][4];
@@ -1032,7 +1126,7 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
                         *reinterpret_cast<float4*>(p.Z + (((size_t)mi * p.S + d->split) * P + d->rows[m]) * p.I + n0) =
                             *reinterpret_cast<const float4*>(red + ((size_t)mi * MP + m) * GRED + 4 * lane);
                 named_sync(1, CT);
-                if (threadIdx.x == 0) enqueue(0, u, b);
+                if (warp == 0) enqueue(0, u, d);
             } else if (!down) {                // the whole of K in this item: the SwiGLU now, then the entry's release
                 const int n0 = b * 128 + 4 * lane;
                 for (int m = warp; m < nm; m += GWARPS) {
@@ -1058,11 +1152,11 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
                     *reinterpret_cast<float4*>(p.y + (size_t)d->rows[m] * p.D + n0) = o;
                 }
                 named_sync(1, CT);
-                if (threadIdx.x == 0) enqueue(1, u, b);
+                if (warp == 0) enqueue(1, u, d);
             }
             named_sync(1, CT);   // red and the descriptor are free for the next item
         }
-        if (threadIdx.x == 0) enqueue(2, 0, 0);
+        if (warp == 0) enqueue(2, 0, nullptr);
     }
     // the last CTA to leave resets the entries' readiness (every producer of every CTA is past its waits by then)
     named_sync(3, GWARPS * 32 + 32);
@@ -1439,8 +1533,9 @@ int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, c
     ESP_REQUIRE(D % 128 == 0 && I % 128 == 0 && S >= 1 && D / 16 >= S && D / 128 <= 256, ESP_ERR_INVALID,
                 "moe_layer: shapes");
     ESP_REQUIRE(S == 1 || Z, ESP_ERR_SCRATCH, "moe_layer: split partials need Z");
-    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && slots >= 1 && slots <= 32 && n_routed <= slots && rows >= 0,
-                ESP_ERR_INVALID, "moe_layer: limits (32 members, 32 slots)");
+    ESP_REQUIRE(maxm >= 1 && maxm <= 32 && maxu >= 1 && slots >= 1 && slots <= 32 && n_routed <= slots && rows >= 0 &&
+                    rows <= 32,
+                ESP_ERR_INVALID, "moe_layer: limits (32 rows, 32 members, 32 slots)");
     ESP_REQUIRE(out_dtype >= 0 && out_dtype <= 2, ESP_ERR_INVALID, "moe_layer: dtype");
     int km = 0, kmax = 0;
     for (int t = 0; t < 3; ++t) {
