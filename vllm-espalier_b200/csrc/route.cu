@@ -195,6 +195,7 @@ __device__ void group_block(const int* sh_pick, int n, int slots, int n_ids, int
 __device__ void group_distinct(const int* sh_pick, int R, int slots, int n_ids, int* __restrict__ uids,
                                int* __restrict__ ucount, int* __restrict__ members, int maxm, int maxu) {
     __shared__ unsigned sh_mask[MAX_E];
+    __shared__ int sh_place[MAX_E];
     __shared__ int warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int e = threadIdx.x; e < n_ids; e += blockDim.x) sh_mask[e] = 0u;
@@ -233,22 +234,26 @@ __device__ void group_distinct(const int* sh_pick, int R, int slots, int n_ids, 
     }
     __syncthreads();
     int place = warp_tot[warp] + inc - used;
-    for (int q = 0; q < per && q < 2; ++q) {
-        unsigned m = mk[q];
+    for (int q = 0; q < per && q < 2; ++q) {   // an id's entry: its id and the padding after its members
+        const unsigned m = mk[q];
         if (m == 0u) continue;
         const int e = threadIdx.x * per + q;
+        sh_place[e] = place;
         if (place < maxu) {
             uids[place] = e;
-            int j = 0;
-            for (; m != 0u && j < maxm; m &= m - 1u) {
-                const int r = __ffs(m) - 1;
-                int sl = 0;
-                while (sh_pick[r * slots + sl] != e) ++sl;     // present: the row's bit is set
-                members[place * maxm + j++] = r * 32 + sl;
-            }
-            for (; j < maxm; ++j) members[place * maxm + j] = -1;
+            for (int j = __popc(m); j < maxm; ++j) members[place * maxm + j] = -1;
         }
         ++place;
+    }
+    __syncthreads();
+    // the members, one pick a thread: a pick of row r is its id's member number popc(rows of the id before r)
+    for (int i = threadIdx.x; i < R * slots; i += blockDim.x) {
+        const int e = sh_pick[i];
+        if (e < 0 || e >= n_ids) continue;
+        const int r = i / slots;
+        const int j = __popc(sh_mask[e] & ((1u << r) - 1u));
+        const int at = sh_place[e];
+        if (at < maxu && j < maxm) members[at * maxm + j] = r * 32 + (i - r * slots);
     }
 }
 
@@ -259,44 +264,48 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
                                                    int* __restrict__ counter, int* __restrict__ pick_out,
                                                    float* __restrict__ wts_out, int* __restrict__ uids,
                                                    int* __restrict__ ucount, int* __restrict__ members, int maxm,
-                                                   int maxu) {
+                                                   int maxu, int rpc) {
     __shared__ int last;
     __shared__ int sh_pick[MAX_PICKS];
+    extern __shared__ float sh_logit[];    // [R][C], the last CTA's copy of the logits
     pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int has = shared_id >= 0;
     const int C = E + has;                 // logit columns: experts, then the shared gate
     const int slots = k + has;
-    const int c = blockIdx.x * RW + warp;      // a warp a (logit column, RB rows)
-    const int r0 = blockIdx.y * RB;
+    const int c = blockIdx.x * RW + warp;      // a warp a logit column, rpc rows a CTA, RB at a time
+    const int r0 = blockIdx.y * rpc;
     const T* w = c < E ? gate + (size_t)c * H : sgate;
     uint4 uw[MAXC];
     if (c < C) load_w<T>(w, H, lane, uw);      // the router's weights overlap the previous kernel's tail
     pdl_wait();
-    if (c < C) {
-        const int nr = min(RB, R - r0);
-        double acc[RB];
-        logits64<T>(x + (size_t)r0 * x_stride, x_stride, nr, w, uw, H, lane, acc);
+    if (c < C)
+        for (int rb = r0; rb < min(R, r0 + rpc); rb += RB) {
+            const int nr = min(RB, R - rb);
+            double acc[RB];
+            logits64<T>(x + (size_t)rb * x_stride, x_stride, nr, w, uw, H, lane, acc);
 #pragma unroll
-        for (int r = 0; r < RB; ++r)
-            if (r < nr && lane == 0) logits[(size_t)(r0 + r) * C + c] = c < E ? round_bf16_d(acc[r]) : (float)acc[r];
-    }
+            for (int r = 0; r < RB; ++r)
+                if (r < nr && lane == 0) logits[(size_t)(rb + r) * C + c] = c < E ? round_bf16_d(acc[r]) : (float)acc[r];
+        }
     __syncthreads();
     if (threadIdx.x == 0) {
         last = arrive_acq_rel(counter) == (int)(gridDim.x * gridDim.y) - 1;
     }
     __syncthreads();
     if (!last) return;
+    for (int i = threadIdx.x; i < R * C; i += RT) sh_logit[i] = __ldcg(logits + i);   // one round of loads
+    __syncthreads();
 
     // per row (a warp a row): top-k of the bf16 logits, lowest id on ties (a warp max over the keys a pick, the
     // winner's key cleared); lane t keeps pick t; weights exp(l_t - l_0) / sum, summed in pick order
     for (int r = warp; r < R; r += RW) {
-        const float* lr = logits + (size_t)r * C;
+        const float* lr = sh_logit + (size_t)r * C;
         uint32_t key[MAX_E / 32];
 #pragma unroll
         for (int q = 0; q < MAX_E / 32; ++q) {
             const int e = lane + 32 * q;
-            key[q] = e < E ? topk_key(__ldcg(lr + e), e) : 0u;
+            key[q] = e < E ? topk_key(lr[e], e) : 0u;
         }
         int my_id = 0;
         float my_v = 0.f;
@@ -325,7 +334,7 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
         if (has && lane == 0) {
             pick_out[r * slots + k] = shared_id;
             sh_pick[r * slots + k] = shared_id;
-            wts_out[r * slots + k] = 1.f / (1.f + expf(-__ldcg(lr + E)));
+            wts_out[r * slots + k] = 1.f / (1.f + expf(-lr[E]));
         }
     }
     __syncthreads();   // the picks are in sh_pick (written beside pick_out above)
@@ -413,16 +422,30 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
                 ESP_ERR_INVALID, "route_group: rows must be 16-byte aligned");
     ESP_REQUIRE(maxm >= R && maxu >= 1, ESP_ERR_INVALID, "route_group: members must hold R entries an expert");
     const int C = E + has;
+    // one wave: a CTA an SM (the kernel's registers allow one), the row pairs spread over what the columns leave
+    const int gx = (C + RW - 1) / RW, pairs = (R + RB - 1) / RB;
+    const int ry = std::max(1, std::min(pairs, device_sms() / gx));
+    const int ppc = (pairs + ry - 1) / ry;    // row pairs a CTA
+    const dim3 grid((unsigned)gx, (unsigned)((pairs + ppc - 1) / ppc));
+    const size_t smem = (size_t)R * C * sizeof(float);
+    static bool opted[2] = {false, false};
+    const int ti = x_dtype == ESP_DTYPE_BF16 ? 0 : 1;
+    if (!opted[ti]) {
+        const int rc0 = ti == 0 ? allow_smem(route_kernel<__nv_bfloat16>, (size_t)32 * MAX_E * sizeof(float))
+                                : allow_smem(route_kernel<__half>, (size_t)32 * MAX_E * sizeof(float));
+        if (rc0) return rc0;
+        opted[ti] = true;
+    }
     int rc;
     if (x_dtype == ESP_DTYPE_BF16)
-        rc = launch(route_kernel<__nv_bfloat16>, dim3((C + RW - 1) / RW, (R + RB - 1) / RB), dim3(RT), 0, stream, true,
+        rc = launch(route_kernel<__nv_bfloat16>, grid, dim3(RT), smem, stream, true,
                     static_cast<const __nv_bfloat16*>(x), x_stride, R, H, static_cast<const __nv_bfloat16*>(gate), E,
                     static_cast<const __nv_bfloat16*>(sgate), k, shared_id, logits, counter, pick_out, wts_out, uids,
-                    ucount, members, maxm, maxu);
+                    ucount, members, maxm, maxu, ppc * RB);
     else
-        rc = launch(route_kernel<__half>, dim3((C + RW - 1) / RW, (R + RB - 1) / RB), dim3(RT), 0, stream, true, static_cast<const __half*>(x), x_stride,
+        rc = launch(route_kernel<__half>, grid, dim3(RT), smem, stream, true, static_cast<const __half*>(x), x_stride,
                     R, H, static_cast<const __half*>(gate), E, static_cast<const __half*>(sgate), k, shared_id, logits,
-                    counter, pick_out, wts_out, uids, ucount, members, maxm, maxu);
+                    counter, pick_out, wts_out, uids, ucount, members, maxm, maxu, ppc * RB);
     if (rc) return rc;
     return ok();
 }
