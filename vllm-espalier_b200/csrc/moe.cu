@@ -189,6 +189,46 @@ __device__ __forceinline__ void dispatch_units(int cb, int K, const uint32_t* st
     }
 }
 
+// All stages of one item for one matrix, codebook and width fixed (the one-launch layer): the (codebook, width)
+// dispatch happens once an item, not once a stage. The item's first stage has been waited for by the caller.
+template <int CB, int K, int NTG, int GST, int STW, int UWM, int SLW>
+__device__ __forceinline__ bool item_stages(const uint32_t* smem, uint64_t* full, uint64_t* empty, int& slot, int& phase,
+                                            int n, int grp, int wl, int lane, int ntg, float (&acc)[2][NTG][4]) {
+    for (int i0 = 0;; i0 += GUPS) {
+        if (i0 > 0 && !mbar_wait(&full[slot], phase)) return false;
+        const uint32_t* st = smem + (size_t)slot * STW;
+        const int m0 = min(GUPS, n - i0);
+        if constexpr (CB > 0)
+            if (m0 > 0) stage_units<CB, K, NTG>(st, st + GUPS * UWM, 0, m0, UWM, SLW, grp, wl, lane, ntg, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == GST) {
+            slot = 0;
+            phase ^= 1;
+        }
+        if (i0 + GUPS >= n) return true;
+    }
+}
+
+template <int NTG, int KCAP, int GST, int STW, int UWM, int SLW>
+__device__ __forceinline__ bool dispatch_item(int cb, int K, const uint32_t* smem, uint64_t* full, uint64_t* empty,
+                                              int& slot, int& phase, int n, int grp, int wl, int lane, int ntg,
+                                              float (&acc)[2][NTG][4]) {
+    switch (cb * 16 + K) {
+#define ESP_IT_CASE(CB_, K_)                                                                                      \
+    case CB_ * 16 + K_:                                                                                           \
+        if constexpr (K_ <= KCAP)                                                                                 \
+            return item_stages<CB_, K_, NTG, GST, STW, UWM, SLW>(smem, full, empty, slot, phase, n, grp, wl, lane, \
+                                                                 ntg, acc);                                        \
+        break;
+        ESP_FOR_EACH_CASE(ESP_IT_CASE)
+#undef ESP_IT_CASE
+        default: break;
+    }
+    report(ESP_ERR_UNSUPPORTED);    // validated on the host; the stages are still consumed, never a trap
+    return item_stages<0, 1, NTG, GST, STW, UWM, SLW>(smem, full, empty, slot, phase, n, grp, wl, lane, ntg, acc);
+}
+
 // The gate/up epilogue of one member row's 4 columns of this lane (experts.cu:120-162, act_mode 1): sums times the
 // codebook steps, H, * h * svh, silu(g) * u, * suh_d (never contracted into the butterfly), H, * h -> fp16 xd.
 // The lane's 4 fp16 scales of a 128-column block (8 bytes), loaded ahead of the epilogue that needs them.
@@ -1058,43 +1098,30 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
             const ItemDesc* d = &desc[di];
             int nkt = 0, nmats = 0, ntg = 0, mcb = 0, mK = 0, item = -1;
             Scales4 sc{};
-            for (int i0 = 0;; i0 += GUPS) {
-                if (!mbar_wait(&full[slot], phase)) {
-                    item = -1;
-                    break;
-                }
-                if (i0 == 0) {
-                    item = d->it;
-                    nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
-                    const bool mB = nmats == 2 && grp == 1;
-                    mcb = mB ? d->cb1 : d->cb0;
-                    mK = mB ? d->K1 : d->K0;
-                    if (item >= 0) {
-                        const int n0s = d->b * 128 + 4 * lane;
-                        if (item >= n_gu) {
-                            sc.d = ld_scales4(p.svh_d, d->e, p.D, n0s);
-                        } else if (p.S == 1) {
-                            sc.g = ld_scales4(p.svh_g, d->e, p.I, n0s);
-                            sc.u = ld_scales4(p.svh_u, d->e, p.I, n0s);
-                            sc.d = ld_scales4(p.suh_d, d->e, p.I, n0s);
-                        }
-                    }
-                }
-                const int n = nmats * nkt;
-                const uint32_t* st = smem + (size_t)slot * STAGE_W;
-                const int m0 = min(GUPS, n - i0);
-                if (m0 > 0)
-                    dispatch_units<NTG, KCAP>(mcb, mK, st, st + GUPS * UNIT_WMAX, 0, m0, UNIT_WMAX, SLICE_W, grp, wl,
-                                              lane, ntg, acc);
+            if (!mbar_wait(&full[slot], phase)) break;   // the item's first stage (or the end marker)
+            item = d->it;
+            if (item < 0) {                               // the end marker: release its stage and leave
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
-                if (++slot == GSTAGES) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-                if (i0 + GUPS >= n) break;
+                break;
             }
-            if (item < 0) break;
+            nkt = d->nkt; nmats = d->nmats; ntg = (d->nm + 7) / 8;
+            {
+                const bool mB = nmats == 2 && grp == 1;
+                mcb = mB ? d->cb1 : d->cb0;
+                mK = mB ? d->K1 : d->K0;
+                const int n0s = d->b * 128 + 4 * lane;
+                if (item >= n_gu) {
+                    sc.d = ld_scales4(p.svh_d, d->e, p.D, n0s);
+                } else if (p.S == 1) {
+                    sc.g = ld_scales4(p.svh_g, d->e, p.I, n0s);
+                    sc.u = ld_scales4(p.svh_u, d->e, p.I, n0s);
+                    sc.d = ld_scales4(p.suh_d, d->e, p.I, n0s);
+                }
+            }
+            if (!dispatch_item<NTG, KCAP, GSTAGES, STAGE_W, UNIT_WMAX, SLICE_W>(mcb, mK, smem, full, empty, slot, phase,
+                                                                                 nmats * nkt, grp, wl, lane, ntg, acc))
+                break;
 
             const int col = wl * 16 + g;
             for (int gi = 0; gi < 2; ++gi) {
