@@ -274,13 +274,16 @@ def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float, rank
                        "touched_mb_per_layer": nbytes / layers / 1e6 if nbytes else None, "weight_gbs": gbs,
                        "hbm_frac": gbs / peak if gbs else None}
         st.graph = None
-    how = ("fused routing + 3 expert launches a layer" if world == 1 else
+    __graft_entry__.load_package()
+    from vllm_espalier_b200._env import MOE_ONE_LAUNCH as one
+    how = (f"fused routing, rot_in and {'one fused expert launch' if one else 'two fused expert launches'} a layer"
+           if world == 1 else
            f"expert parallel over {world} GPUs: local routing, NCCL all_to_all dispatch of rows and picks, local "
            f"experts, all_to_all of per-slot rows back, slot-ordered combine")
     return {"workload": f"BASELINE configs[2]: {layers} MoE layers a step (256 experts 1/2/3-bit E2M1/int5, int6 "
                         f"shared, top-8 router), {how.strip()}, graph replay",
             "layers": layers, "world": world, "scaling": "weak (R rows a rank)" if world > 1 else None,
-            "launches_per_layer": 4 if world == 1 else None, "batches": res}
+            "launches_per_layer": (3 if one else 4) if world == 1 else None, "batches": res}
 
 
 # ---------------------------------------------------------------------------------------------------------------
