@@ -50,6 +50,8 @@ class Dense:
             raise ValueError("all matrices of a dense layer share their input width")
         self.groups = []                       # launches: (matrix indices, k2, kernel cb)
         for i, m in enumerate(self.mats):
+            if m.cb not in KERNEL_CB:   # esp_grid 2 (E4M3) has no decode kernel, in the reference either
+                raise NotImplementedError(f"matrix {i}: grid code {m.cb} has no decode kernel")
             key = (2 * m.K, KERNEL_CB[m.cb])
             if self.groups and (self.groups[-1][1], self.groups[-1][2]) == key and len(self.groups[-1][0]) < 4:
                 self.groups[-1][0].append(i)
