@@ -1,4 +1,4 @@
-"""Expert parallelism host logic on CPU ranks (gloo, world size 2): the dispatch / local-table / give-back path of
+"""Expert parallelism host logic on CPU ranks (gloo, world sizes 2, 4 and 8): the dispatch / local-table / give-back path of
 vllm_espalier_b200.ep with a stand-in expert function must deliver every routed slot's y row to its home rank, so that
 the slot-ordered combine gives the same bits as one process holding every expert.
 
@@ -91,8 +91,8 @@ def _worker(rank: int, world: int, port: int, q):
         dist.destroy_process_group()
 
 
-def test_ep_exchange_matches_one_rank_bitwise():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_exchange_matches_one_rank_bitwise(world):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()

@@ -1,8 +1,9 @@
-"""Expert-parallel MoE layer on 2 GPUs (NCCL): each rank's EPLayer output must equal, bit for bit, the single-GPU
-fused path (route + routed2) on a layer holding every expert, for the same rows. Skipped with fewer than 2 GPUs.
+"""Expert-parallel MoE layer on 2, 4 and 8 GPUs (NCCL): each rank's EPLayer output must equal, bit for bit, the
+single-GPU fused path (route + routed2) on a layer holding every expert, for the same rows. Each world size is skipped
+on a box with fewer GPUs.
 
-One case biases the router so that one expert is picked by every row: 64 rows of a 2-rank window then give that
-expert 64 members, more than a grouping entry holds (32), which exercises the chunked grouping."""
+One case biases the router so that one expert is picked by every row: the 32 rows of every rank then give that expert
+32 x world members, more than a grouping entry holds (32), which exercises the chunked grouping."""
 from __future__ import annotations
 
 import os
@@ -79,12 +80,12 @@ def _worker(rank, world, port, R, bias, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("R,bias", [(3, False), (32, False), (32, True)])
-def test_ep_two_gpus_bitwise_equal_to_one_gpu(R, bias):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_ep_bitwise_equal_to_one_gpu(world, R, bias):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()
