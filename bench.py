@@ -519,8 +519,8 @@ def cpu_baseline(blocks, R: int, layers: int, seconds: float = 10.0) -> dict:
     el = time.perf_counter() - t0
     per_block = el / n_blocks
     return {"value": R / (per_block * layers), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n_blocks} of the step's {layers} blocks at batch {R} ({el:.1f} s; decode {decode_s:.1f} s), "
-                      f"scaled to one {layers}-block step",
+            "sample": f"{n_blocks} q/k/v/o blocks at batch {R} (the step's {layers} blocks in turn; {el:.1f} s, of "
+                      f"which trellis decode {decode_s:.1f} s), scaled to one {layers}-block step",
             "block_ms": per_block * 1e3}
 
 
