@@ -251,6 +251,13 @@ int esp_combine(const float* y, const float* wts, float* out, int rows, int D, i
 int esp_ep_combine(const float* recv_y, const int* pick, const float* wts, void* out, void* out_shared, int out_dtype,
                    int R, int D, int slots, int n_routed, int E_routed, int world, int rank, void* stream);
 
+/*
+ * Diagnostic: the bounded wait of the expert kernels on a device flag (int32), on its own. One thread waits until
+ * *flag >= need, giving up after 0.2 s (ESP_ERR_TIMEOUT in esp_device_status); *result = 1 if reached, 0 if it gave
+ * up. For tests of the timeout path (a flag that nothing sets); no counterpart in the reference.
+ */
+int esp_wait_flag(const int* flag, int need, int* result, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

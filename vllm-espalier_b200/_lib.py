@@ -56,6 +56,7 @@ SIGNATURES = {
     "esp_down_combine": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, P]),
     "esp_combine": (I, [P, P, P, I, I, I, P]),
     "esp_ep_combine": (I, [P, P, P, P, P, I, I, I, I, I, I, I, I, P]),
+    "esp_wait_flag": (I, [P, I, P, P]),
     "esp_moe_layer": (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P, P, I, I, P, P, I, I, I, I, I, I,
                           P, P, P, P, P, P, I, P]),
     "esp_moe_layer_counters": (S, [I, I, I, I]),

@@ -754,6 +754,13 @@ __device__ __forceinline__ bool wait_smem_gt(const volatile int* w, int v) {
     return false;
 }
 
+// The layer kernel's readiness wait on its own: one thread waits until *flag >= need (bounded by time; on giving up
+// ESP_ERR_TIMEOUT is recorded in the status word) and writes 1 (reached) or 0 (gave up) to *result. It lets a test run
+// the timeout path on a flag that nothing sets and check that the host reads the status and the context stays usable.
+__global__ void wait_flag_kernel(const int* flag, int need, int* result) {
+    if (threadIdx.x == 0) *result = wait_ready(flag, need) ? 1 : 0;
+}
+
 template <int NTG, int KCAP>
 __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constant__ LayerParams p) {
     constexpr int GSTAGES = gstages(NTG, KCAP);
@@ -1648,6 +1655,12 @@ int esp_ep_combine(const float* recv_y, const int* pick, const float* wts, void*
     if (int rc = launch(ep_combine_kernel, dim3((unsigned)R, (unsigned)(D / 128)), dim3(32), 0, stream, true, recv_y, pick,
                         wts, out, out_shared, out_dtype, R, D, slots, n_routed, E_routed, world, rank))
         return rc;
+    return ok();
+}
+
+int esp_wait_flag(const int* flag, int need, int* result, void* stream) {
+    ESP_REQUIRE(flag && result, ESP_ERR_INVALID, "wait_flag: null pointer");
+    if (int rc = launch(wait_flag_kernel, dim3(1), dim3(32), 0, stream, false, flag, need, result)) return rc;
     return ok();
 }
 
