@@ -125,3 +125,13 @@ def test_switch_salting(monkeypatch):
     monkeypatch.setenv("ESPALIER_PREFILL_MODE", "gemm")
     b = h(Cfg())
     assert a != b and len(a) == len(b) == 16 and h._esp
+
+
+def test_register_patches_vllm_once(cfg_mod):
+    from vllm.config import VllmConfig
+    from vllm.model_executor.layers.quantization import get_quantization_config
+    plugin.register()
+    first = VllmConfig.compute_hash
+    plugin.register()
+    assert VllmConfig.compute_hash is first and first._esp
+    assert get_quantization_config("espalier") is cfg_mod.EspalierConfig
