@@ -14,9 +14,10 @@
 // correctly rounded logits' choice. Top-k compares bf16 logit values (exp is monotone), so the choice does not depend
 // on the exponential's last bit.
 //
-// B200 layout: a warp a (logit column, 2 rows) over a 2-D grid (E experts + the shared gate by row pairs), all of its
-// loads in flight at once; the last CTA to arrive (acq_rel counter) does the per-row selection (a warp a row) and the
-// grouping, then resets the counter.
+// B200 layout: a warp a logit column (E experts + the shared gate), one wave of CTAs (one an SM) over a 2-D grid of
+// column groups x row-pair groups, each CTA looping over its row pairs with all of a pair's loads in flight at once;
+// the last CTA to arrive (acq_rel counter) stages the logits in shared memory, does the per-row selection (a warp a
+// row) and the grouping (members written in parallel over the picks), then resets the counter.
 #include <cuda_runtime.h>
 
 #include <algorithm>
