@@ -39,7 +39,7 @@ BITS, GRID, KCB = 4, 3, 6            # 4-bit, esp_grid code 3 = int5, kernel cod
 
 
 def block_bytes() -> int:
-    """Algorithmic bytes of one block: trellis + suh + svh of q, k, v and o (9,472,000)."""
+    """Algorithmic bytes of one block: trellis + suh + svh of q, k, v and o (9,472,000 for the 4-bit config-2 block)."""
     qkv = HIDDEN * sum(QKV_N) * BITS // 8 + 3 * HIDDEN * 2 + sum(QKV_N) * 2
     o = O_IN * HIDDEN * BITS // 8 + O_IN * 2 + HIDDEN * 2
     return qkv + o
