@@ -63,6 +63,10 @@ def test_host_validation_without_gpu():
     args[17] = 0         # counters too small
     assert lib.esp_dense(*args) == _lib.ESP_ERR_SCRATCH
     assert lib.esp_dense(None, *args[1:]) == _lib.ESP_ERR_INVALID
+    # the diagnostic wait checks its pointers before any launch
+    assert lib.esp_wait_flag(None, 1, C.c_void_p(16), None) == _lib.ESP_ERR_INVALID
+    assert lib.esp_wait_flag(C.c_void_p(16), 1, None, None) == _lib.ESP_ERR_INVALID
+    assert b"null" in lib.esp_last_error()
 
 
 def test_ext_surface_names():
