@@ -1,7 +1,7 @@
 """Grouped routed experts: one MoE layer for up to ROWS tokens (the reference's vllm_espalier/experts.py surface:
 KERNEL_CB, COMPILED, ext, tile_config, Layer, prepare, Scratch, scratch, routed, route, windows, routed2, dequant).
 
-B200 pipeline of routed2 (4 launches, the reference's takes 6):
+B200 pipeline of routed2 (3 launches by default, the reference's takes 6):
 
   route / group_shared  the pick / weight tables with the shared expert as one more slot, and the grouping (distinct
                         experts in id order, members in (row, slot) order), on the device, no host sync
@@ -12,6 +12,9 @@ B200 pipeline of routed2 (4 launches, the reference's takes 6):
   moe_down              down of every distinct expert, y = H(.) * svh_d, and the routing-weighted sum over the routed
                         slots in slot order plus the gated shared slot, written in the model's dtype by the last slot
                         of each row to finish
+  moe_layer             (default; ESPALIER_MOE_FUSED=0 runs moe_gateup then moe_down instead) both of the above in one
+                        persistent launch: down items wait, bounded, for their expert's SwiGLU blocks; same sums, same
+                        bits as the two launches
 
 Every sum runs in a fixed order that depends on the shapes only, so a token's output never depends on the other
 tokens in the window, and nothing allocates during a forward, so CUDA graphs capture it. Trellises are read in place
