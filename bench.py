@@ -475,10 +475,10 @@ def time_e2e(step: Step, steps: int, warmup: int, dist, dev) -> tuple[float, int
 
 def cpu_baseline(blocks, R: int, layers: int, seconds: float = 10.0) -> dict:
     """The reference's decode-then-matmul path (vllm_espalier/ops.py:45-51: decode W, H(x suh), x @ W, H * svh)
-    restated on the host: trellis decode by the C oracle (OpenMP, all cores), matmul by torch on all cores. Timed on a
-    bounded sample of whole blocks of this workload, scaled to the step."""
+    restated on the host: trellis decode by the C oracle's word-window decode straight to fp32 (OpenMP, all cores;
+    bit-identical to its bit-serial restatement), matmul by torch on all cores. Timed on a bounded sample of whole
+    blocks of this workload, scaled to the step."""
     sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
     import oracle as O
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -500,14 +500,14 @@ def cpu_baseline(blocks, R: int, layers: int, seconds: float = 10.0) -> dict:
             ys = []
             for T, su, sv in qkv_host:
                 td = time.perf_counter()
-                W = torch.from_numpy(O.dequant(T, BITS, KCB).astype(np.float32))
+                W = torch.from_numpy(O.dequant_f32(T, BITS, KCB))
                 decode_s += time.perf_counter() - td
                 xh = had(x * torch.from_numpy(su).float()).half().float()
                 ys.append(had(xh @ W) * torch.from_numpy(sv).float())
             yq = torch.cat(ys, 1).to(torch.bfloat16).float()
             (T, su, sv), = o_host
             td = time.perf_counter()
-            W = torch.from_numpy(O.dequant(T, BITS, KCB).astype(np.float32))
+            W = torch.from_numpy(O.dequant_f32(T, BITS, KCB))
             decode_s += time.perf_counter() - td
             xh = had(yq[:, :O_IN] * torch.from_numpy(su).float()).half().float()
             x = (had(xh @ W) * torch.from_numpy(sv).float()).to(torch.bfloat16).float()

@@ -234,6 +234,45 @@ int orc_dequant(const int16_t* T, int Kin, int N, int K, int cb, uint16_t* W) {
 }
 
 /* ------------------------------------------------------------------------------------------------------------ */
+/* orc_dequant widened to fp32, for the timed CPU baseline (the reference's decode-then-matmul path restated on the */
+/* host): the same states, each cut from a 64-bit window of two stream words instead of bit by bit, and the        */
+/* codebook as an fp32 table, so the host decode is not a bit-serial strawman. tests/test_oracle.py checks it      */
+/* against orc_dequant for every compiled (codebook, width) pair, bit for bit.                                     */
+/* ------------------------------------------------------------------------------------------------------------ */
+int orc_dequant_f32(const int16_t* T, int Kin, int N, int K, int cb, float* W) {
+    if (Kin % 16 || N % 16 || K < 1 || K > 8) return -1;
+    uint16_t* tab = (uint16_t*)malloc(65536 * sizeof(uint16_t));
+    float* ftab = (float*)malloc(65536 * sizeof(float));
+    if (!tab || !ftab) { free(tab); free(ftab); return -2; }
+    orc_codebook_table(cb, tab);
+    if (tab[0] == 0xffffu && cb != 1) { free(tab); free(ftab); return -3; }
+    for (int i = 0; i < 65536; ++i) ftab[i] = orc_h2f(tab[i]);
+    int off[256];
+    for (int p = 0; p < 256; ++p) {
+        int r, c;
+        orc_value_pos(p, &r, &c);
+        off[p] = r * N + c;
+    }
+    const int KT = Kin / 16, NT = N / 16, TW = 8 * K, nbits = 256 * K;
+#pragma omp parallel for schedule(static)
+    for (int kt = 0; kt < KT; ++kt)
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint32_t* w = (const uint32_t*)(T + ((size_t)kt * NT + nt) * 2 * TW);
+            float* out = W + (size_t)kt * 16 * N + nt * 16;
+            for (int p = 0; p < 256; ++p) {
+                int b = (p + 1) * K - 16;                       /* the state's first stream bit (circular) */
+                if (b < 0) b += nbits;
+                const int wi = b >> 5, sh = b & 31;
+                const uint64_t x = ((uint64_t)w[wi] << 32) | w[(wi + 1) % TW];   /* 64 stream bits, MSB first */
+                out[off[p]] = ftab[(x >> (48 - sh)) & 0xffffu];
+            }
+        }
+    free(tab);
+    free(ftab);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------------------------------------------ */
 /* Hadamard-128 with the reference's butterfly order (dense.cu:43-54): lane L holds v[4L..4L+3]; H4 in registers,  */
 /* then xor-partner stages 1, 2, 4, 8, 16 across lanes (lower lane a + b, upper lane a - b).                       */
 /* ------------------------------------------------------------------------------------------------------------ */

@@ -39,7 +39,8 @@ def _load():
         "orc_mcg": (C.c_uint16, [C.c_uint32]), "orc_codebook": (C.c_uint16, [i, C.c_uint32]),
         "orc_codebook_table": (None, [i, P]), "orc_int_step": (f, [i]),
         "orc_state": (C.c_uint32, [P, i, i]), "orc_states": (None, [P, i, i, i, P]),
-        "orc_dequant": (i, [P, i, i, i, i, P]), "orc_fwht128": (None, [P]),
+        "orc_dequant": (i, [P, i, i, i, i, P]), "orc_dequant_f32": (i, [P, i, i, i, i, P]),
+        "orc_fwht128": (None, [P]),
         "orc_rotate": (None, [P, i, i, P, P]), "orc_dense": (None, [P, P, i, i, i, P, f, P]),
         "orc_had": (None, [P, i, i, P, P, P]), "orc_router_logit": (d, [P, P, i]),
         "orc_group": (i, [P, i, i, i, P, P, i, i]),
@@ -124,6 +125,18 @@ def dequant(T: np.ndarray, K: int, cb: int) -> np.ndarray:
     if rc:
         raise ValueError(f"orc_dequant: error {rc}")
     return W.view(np.float16)
+
+
+def dequant_f32(T: np.ndarray, K: int, cb: int) -> np.ndarray:
+    """dequant's values widened to float32 [Kin, N], through the word-window decode (the timed CPU baseline's)."""
+    T = np.ascontiguousarray(T, dtype=np.int16)
+    KT, NT, L = T.shape
+    assert L == 16 * K, (T.shape, K)
+    W = np.empty((KT * 16, NT * 16), np.float32)
+    rc = lib().orc_dequant_f32(_p(T), KT * 16, NT * 16, K, cb, _p(W))
+    if rc:
+        raise ValueError(f"orc_dequant_f32: error {rc}")
+    return W
 
 
 def int_step(cb: int) -> float:

@@ -170,3 +170,12 @@ def test_route_ties_lowest_id_and_order():
         assert lb[r, rest].max() <= vals.min()
         assert pick[r, 8] == 256
         assert abs(float(wts[r, :8].sum()) - 1) < 1e-6
+
+
+@pytest.mark.parametrize("cb,k2", C.COMPILED)
+def test_word_window_decode_matches_bit_serial(cb, k2):
+    """The timed CPU baseline's decode (64-bit word windows, fp32 out) gives the oracle's weights bit for bit."""
+    T = C.trellis(("f32-decode", cb, k2), 64, 256, k2 // 2)
+    want = O.dequant(T, k2 // 2, cb).astype(np.float32)
+    got = O.dequant_f32(T, k2 // 2, cb)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
