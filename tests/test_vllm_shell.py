@@ -1,7 +1,7 @@
 """The vLLM-facing pieces on CPU (skipped where vLLM cannot be imported): the "espalier" quantization config's
 checkpoint discovery (the reference's tests/test_config.py cases against its config.py), EspLinearMethod's weight
-loading into per-shard EspMatrix objects in vLLM's shard order (the reference's linear.py), and the switch salting of
-vLLM's compile-cache hash."""
+loading into per-shard EspMatrix objects in vLLM's shard order (the reference's linear.py), EspMoEMethod's per-expert
+loading (the reference's moe.py), and the switch salting of vLLM's compile-cache hash."""
 from __future__ import annotations
 
 import json
@@ -12,6 +12,7 @@ import torch
 from helpers import LM, write_checkpoint
 
 from vllm_espalier_b200 import plugin
+from vllm_espalier_b200.matrix import SUFFIXES
 
 
 @pytest.fixture(scope="module")
@@ -135,3 +136,58 @@ def test_register_patches_vllm_once(cfg_mod):
     plugin.register()
     assert VllmConfig.compute_hash is first and first._esp
     assert get_quantization_config("espalier") is cfg_mod.EspalierConfig
+
+
+@pytest.fixture(scope="module")
+def moe_mod(cfg_mod):
+    from vllm_espalier_b200 import moe
+    return moe
+
+
+def _expert_weights(c, want_prefix):
+    """(checkpoint name, tensor) of every expert tensor, as vLLM's loader hands them to the layer."""
+    for k in sorted(c.weight_map):
+        if k.startswith(want_prefix) and not k.endswith(".weight"):
+            base, _, suffix = k.rpartition(".")
+            yield k, c.tensors(base)[suffix]
+
+
+def test_moe_method_loads_experts(tmp_path, moe_mod):
+    from vllm_espalier_b200 import checkpoint as ck
+    want = write_checkpoint(tmp_path)
+    c = ck.Checkpoint(tmp_path)
+    m = moe_mod.EspMoEMethod.__new__(moe_mod.EspMoEMethod)       # the config object only feeds vLLM's base class
+    assert m.topk_indices_dtype == torch.int32 and m.is_monolithic == moe_mod.ROUTE
+    layer = torch.nn.Module()
+    m.create_weights(layer, 2, 256, 128, torch.bfloat16)
+    names = list(layer.load_weights(_expert_weights(c, f"{LM}.0.mlp.experts.")))
+    assert set(names) <= {f"{w}_{s}" for w in ("w13", "w2") for s in SUFFIXES}
+    assert "w2_esp_trellis" in names and "w13_esp_grid" in names
+    m.process_weights_after_loading(layer)
+    assert len(layer._esp_experts) == 2 and layer._esp_grouped is None
+    for e, mats in enumerate(layer._esp_experts):
+        for mt, p in zip(mats, ("gate_proj", "up_proj", "down_proj")):
+            assert torch.equal(mt.trellis, want[f"{LM}.0.mlp.experts.{e}.{p}"]["esp_trellis"])
+    assert [(mt.K, mt.cb) for mt in layer._esp_experts[1]] == [(3, 3), (3, 3), (4, 4)]
+
+
+def test_moe_method_errors(tmp_path, moe_mod):
+    from vllm_espalier_b200 import checkpoint as ck
+    write_checkpoint(tmp_path)
+    c = ck.Checkpoint(tmp_path)
+    m = moe_mod.EspMoEMethod.__new__(moe_mod.EspMoEMethod)
+    layer = torch.nn.Module()
+    m.create_weights(layer, 3, 256, 128, torch.bfloat16)               # expert 2 never arrives
+    list(layer.load_weights(_expert_weights(c, f"{LM}.0.mlp.experts.")))
+    with pytest.raises(RuntimeError, match="3 expert matrices missing"):
+        m.process_weights_after_loading(layer)
+    bad = torch.nn.Module()
+    m.create_weights(bad, 2, 256, 128, torch.bfloat16)
+    with pytest.raises(ValueError):
+        list(bad.load_weights([("model.layers.0.mlp.experts.gate_up_proj.weight", torch.zeros(1))]))
+    gelu = torch.nn.Module()
+    m.create_weights(gelu, 2, 256, 128, torch.bfloat16)
+    gelu.activation = "gelu"
+    list(gelu.load_weights(_expert_weights(c, f"{LM}.0.mlp.experts.")))
+    with pytest.raises(NotImplementedError):
+        m.process_weights_after_loading(gelu)

@@ -2,8 +2,8 @@
 
 Which modules are trellis-coded is read from the checkpoint (checkpoint.Checkpoint: every `.esp_trellis` key) when
 vLLM calls maybe_update_config with the model path. Coded dense layers and the LM head get EspLinearMethod (linear.py,
-the fused dense kernel through espalier::dense); everything else stays unquantized. Importing this module needs vLLM;
-the rest of the package does not.
+the fused dense kernel through espalier::dense), coded routed experts EspMoEMethod (moe.py, the grouped pipeline);
+everything else stays unquantized. Importing this module needs vLLM; the rest of the package does not.
 """
 from __future__ import annotations
 
@@ -82,9 +82,8 @@ class EspalierConfig(QuantizationConfig):
         if RoutedExperts and isinstance(layer, RoutedExperts):
             if not self.experts_exl3(prefix):
                 raise ValueError(f"{prefix}: routed experts without EXL3 tensors")
-            raise NotImplementedError(
-                f"{prefix}: coded routed experts run through experts.prepare / route / routed2; this package has no "
-                f"vLLM MoE method (the reference's needs vLLM 0.31's MoE runner)")
+            from .moe import EspMoEMethod
+            return EspMoEMethod(layer.moe_config)
         if isinstance(layer, ParallelLMHead):
             return EspLinearMethod(prefix) if self.is_exl3(prefix) else None
         if isinstance(layer, LinearBase):
