@@ -4,6 +4,7 @@ EspMatrix objects read back bit for bit from sharded safetensors files."""
 from __future__ import annotations
 
 import json
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -120,3 +121,18 @@ def test_single_file_checkpoint_and_e4m3(tmp_path):
     assert m.cb == 2
     with pytest.raises(NotImplementedError):                     # no decode kernel for E4M3, as in the reference
         D.Dense([m])
+
+
+def test_pinned_to_the_reference_key_logic(tmp_path):
+    """tests/golden/checkpoint_keys.json holds the reference's own text_key / is_exl3 / experts_exl3 answers
+    (tests/golden/make_checkpoint_keys.py ran its config.py); this module must give the same for every name."""
+    gold = json.loads((Path(__file__).parent / "golden" / "checkpoint_keys.json").read_text())
+    c = _index(tmp_path, gold["checkpoint_keys"])
+    for name, want in gold["names"].items():
+        assert ck.text_key(name) == want["text_key"], name
+        if want["is_exl3"] == "error":
+            with pytest.raises(ValueError):
+                c.is_exl3(name)
+        else:
+            assert c.is_exl3(name) == want["is_exl3"], name
+        assert c.experts_exl3(name) == want["experts_exl3"], name
