@@ -1,6 +1,8 @@
 """Generate tests/golden/checkpoint_keys.json from the REFERENCE plugin's own key logic (vllm_espalier/config.py:
-text_key, EspalierConfig.maybe_update_config / is_exl3 / experts_exl3), imported from a reference checkout (it needs
-vLLM). tests/test_checkpoint.py pins vllm_espalier_b200.checkpoint against these answers with no reference present.
+text_key, EspalierConfig.maybe_update_config / is_exl3 / experts_exl3; linear.py: shard_order; moe.py: the expert
+tensor name pattern), imported from a reference checkout (it needs vLLM). tests/test_checkpoint.py and
+tests/test_vllm_shell.py pin this package's checkpoint, linear and moe modules against these answers with no reference
+present.
 
 The names are synthetic module and checkpoint names of the kinds the reference handles (decoder layers, fused
 projections, MTP layers, the head, vision modules, routed experts).
@@ -39,6 +41,14 @@ NAMES = [
     "model.vision_tower.layers.0.mlp.fc1", "language_model.model.embed_tokens", "language_model.model.norm",
 ]
 
+SHARDS = [None, "q", "k", "v", [2, 1], [0, 1], 0, 3]
+EXPERT_NAMES = [
+    "model.language_model.layers.0.mlp.experts.7.down_proj.esp_trellis", "experts.0.gate_proj.suh",
+    "layers.3.mlp.experts.12.up_proj.esp_grid", "model.layers.0.mlp.experts.gate_up_proj.weight",
+    "model.layers.0.mlp.experts.3.w1.esp_trellis", "mtp.layers.0.mlp.experts.255.down_proj.svh",
+    "layers.0.mlp.experts.1.down_proj.mul1", "layers.0.mlp.experts.x.up_proj.suh",
+]
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -58,6 +68,15 @@ def main():
         except ValueError:
             exl3 = "error"
         out["names"][n] = {"text_key": text_key(n), "is_exl3": exl3, "experts_exl3": cfg.experts_exl3(n)}
+    # the loaders' own keying: vLLM shard ids -> output order (linear.py), expert tensor names -> (expert, projection,
+    # suffix) (moe.py's name pattern)
+    from vllm_espalier import linear as ref_linear
+    from vllm_espalier import moe as ref_moe
+    out["shard_order"] = [[sh, ref_linear.shard_order(tuple(sh) if isinstance(sh, list) else sh)] for sh in SHARDS]
+    out["expert_names"] = {}
+    for n in EXPERT_NAMES:
+        m = ref_moe._NAME.search(n)
+        out["expert_names"][n] = [int(m.group(1)), m.group(2), m.group(3)] if m else None
     (HERE / "checkpoint_keys.json").write_text(json.dumps(out, indent=1) + "\n")
     print(f"wrote {len(NAMES)} names")
 

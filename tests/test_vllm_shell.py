@@ -5,6 +5,7 @@ loading (the reference's moe.py), and the switch salting of vLLM's compile-cache
 from __future__ import annotations
 
 import json
+from pathlib import Path
 
 import pytest
 import torch
@@ -191,3 +192,14 @@ def test_moe_method_errors(tmp_path, moe_mod):
     list(gelu.load_weights(_expert_weights(c, f"{LM}.0.mlp.experts.")))
     with pytest.raises(NotImplementedError):
         m.process_weights_after_loading(gelu)
+
+
+def test_loader_keying_pinned_to_the_reference(moe_mod, lin):
+    """tests/golden/checkpoint_keys.json holds the reference's own shard_order (linear.py) and expert tensor name
+    parsing (moe.py) answers; the methods here key loaded tensors the same way."""
+    gold = json.loads((Path(__file__).parent / "golden" / "checkpoint_keys.json").read_text())
+    for shard, want in gold["shard_order"]:
+        assert lin.shard_order(tuple(shard) if isinstance(shard, list) else shard) == want, shard
+    for name, want in gold["expert_names"].items():
+        m = moe_mod._EXPERT_TENSOR.search(name)
+        assert ([int(m.group(1)), m.group(2), m.group(3)] if m else None) == want, name
