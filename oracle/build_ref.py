@@ -7,7 +7,7 @@ The sources are compiled where they lie in the reference checkout (nothing is co
 build products land in oracle/_ref/ (git-ignored). The recipe is ours: torch.utils.cpp_extension with explicit sm_100a
 flags, the four translation units the reference's extension is made of (experts.cpp, experts.cu, dense.cu, route.cu).
 
-usage: python oracle/build_ref.py [--reference PATH]     (about 3 minutes on 8 cores)
+usage: python oracle/build_ref.py --reference PATH   (or ESPALIER_REFERENCE=PATH)     (about 3 minutes on 8 cores)
 """
 from __future__ import annotations
 
@@ -40,7 +40,9 @@ def build(reference: Path, verbose: bool = False) -> Path | None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path(os.environ.get("ESPALIER_REFERENCE", "/root/reference")))
+    env = os.environ.get("ESPALIER_REFERENCE")
+    ap.add_argument("--reference", type=Path, default=Path(env) if env else None, required=not env,
+                    help="the reference checkout (default: $ESPALIER_REFERENCE)")
     ap.add_argument("--clean", action="store_true")
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()

@@ -1,20 +1,5 @@
-import sys
-from pathlib import Path
-
+"""Shared fixtures. The import paths (repository root, oracle/, tests/, tests/golden/) come from pyproject.toml."""
 import pytest
-
-ROOT = Path(__file__).resolve().parent.parent
-for p in (ROOT, ROOT / "oracle", ROOT / "tests" / "golden"):
-    if str(p) not in sys.path:
-        sys.path.insert(0, str(p))
-
-import __graft_entry__  # noqa: E402
-
-__graft_entry__.load_package()
-
-
-def pytest_configure(config):
-    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); the parity tests proper")
 
 
 @pytest.fixture(scope="session")

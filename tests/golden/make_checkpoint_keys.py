@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 import tempfile
 from pathlib import Path
@@ -52,7 +53,9 @@ EXPERT_NAMES = [
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    env = os.environ.get("ESPALIER_REFERENCE")
+    ap.add_argument("--reference", type=Path, default=Path(env) if env else None, required=not env,
+                    help="the reference checkout (default: $ESPALIER_REFERENCE)")
     a = ap.parse_args()
     sys.path.insert(0, str(a.reference))
     from vllm_espalier.config import EspalierConfig, text_key   # the reference's own module

@@ -149,7 +149,7 @@ def test_graph_equals_eager_and_counters_zero(dev):
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
-    assert int(d.counters.abs().sum()) == 0
+    assert int(d.ws.counters.abs().sum()) == 0
 
 
 def test_fp32_and_fp16_io(dev):
@@ -164,10 +164,10 @@ def test_fp32_and_fp16_io(dev):
 def test_errors_are_raised(dev):
     ms, x, _ = _layer("int6_single", 512, [256], 7, 8, 1, "bf16", dev)
     d = D.Dense(ms)
-    z, xh = D.scratch(dev, 0, 0)
+    z, xh = d.ws.z, d.ws.xh
     y = torch.empty((1, 256), dtype=torch.bfloat16, device=dev)
     with pytest.raises(RuntimeError, match="unsupported codebook"):
-        _lib.ext().dense(x, [ms[0].trellis], [ms[0].suh], [ms[0].svh], [0], y, xh, z, d.counters, 8, 3)
+        _lib.ext().dense(x, [ms[0].trellis], [ms[0].suh], [ms[0].svh], [0], y, xh, z, d.ws.counters, 8, 3)
     with pytest.raises(RuntimeError, match="1 to 32 rows"):
         big = torch.zeros((33, 512), dtype=torch.bfloat16, device=dev)
-        _lib.ext().dense(big, [ms[0].trellis], [ms[0].suh], [ms[0].svh], [0], y, xh, z, d.counters, 8, 7)
+        _lib.ext().dense(big, [ms[0].trellis], [ms[0].suh], [ms[0].svh], [0], y, xh, z, d.ws.counters, 8, 7)

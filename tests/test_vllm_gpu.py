@@ -28,7 +28,7 @@ def test_linear_method_apply_equals_dense(dev, tmp_path):
         for suffix, t in c.tensors(c.bases[f"layers.3.self_attn.{name}"]).items():
             getattr(layer, suffix).weight_loader(getattr(layer, suffix), t, shard)
     m.process_weights_after_loading(layer)
-    assert layer._esp_dense is not None
+    assert layer.espalier.key is not None
     x = torch.randn(3, 5, 256, generator=torch.Generator().manual_seed(1)).bfloat16().to(dev)
     y = m.apply(layer, x)
     want = D.Dense(c.layer("language_model.model.layers.3.self_attn.qkv_proj", device=dev)).forward(x.reshape(15, 256))

@@ -80,11 +80,11 @@ def test_linear_method_loads_shards_in_vllm_order(tmp_path, monkeypatch, lin):
     assert {n for n, _ in layer.named_parameters()} == set(lin.SUFFIXES)
     _load(layer, c, {"q": "q_proj", "k": "k_proj", "v": "v_proj"}, ["v", "q", "k"])
     m.process_weights_after_loading(layer)
-    assert [x.out_features for x in layer._esp_mats] == [256, 128, 128] and layer._esp_pad == 0
+    assert [x.out_features for x in layer.espalier.mats] == [256, 128, 128] and layer.espalier.pad == 0
     for i, name in enumerate(("q_proj", "k_proj", "v_proj")):
-        assert torch.equal(getattr(layer, f"_esp_t{i}"), want[f"{LM}.3.self_attn.{name}"]["esp_trellis"])
-    assert (layer._esp_mats[2].K, layer._esp_mats[2].cb) == (2, 0)
-    assert layer._esp_dense is None
+        assert torch.equal(getattr(layer, f"esp_trellis_{i}"), want[f"{LM}.3.self_attn.{name}"]["esp_trellis"])
+    assert (layer.espalier.mats[2].K, layer.espalier.mats[2].cb) == (2, 0)
+    assert layer.espalier.key is None
 
 
 def test_linear_method_padding_and_errors(tmp_path, monkeypatch, lin):
@@ -97,7 +97,7 @@ def test_linear_method_padding_and_errors(tmp_path, monkeypatch, lin):
     m.create_weights(layer, 256, [384], 256, 384, torch.bfloat16)        # 128 columns of padding
     _load(layer, c, {None: "o_proj"}, [None])
     m.process_weights_after_loading(layer)
-    assert layer._esp_pad == 128
+    assert layer.espalier.pad == 128
     bad = torch.nn.Module()
     m.create_weights(bad, 512, [256], 512, 256, torch.bfloat16)         # the layer's input width differs
     _load(bad, c, {None: "o_proj"}, [None])
@@ -106,7 +106,7 @@ def test_linear_method_padding_and_errors(tmp_path, monkeypatch, lin):
     head = torch.nn.Module()
     lin.EspLinearMethod("lm_head").create_weights(head, 256, [256], 256, 256, torch.bfloat16)
     lin.EspLinearMethod("lm_head").process_weights_after_loading(head)   # an unloaded drafter head is allowed
-    assert head._esp_mats == [] and head._esp_dense is None
+    assert head.espalier.mats == [] and head.espalier.key is None
     with pytest.raises(RuntimeError):
         empty = torch.nn.Module()
         m.create_weights(empty, 256, [256], 256, 256, torch.bfloat16)
@@ -165,11 +165,11 @@ def test_moe_method_loads_experts(tmp_path, moe_mod):
     assert set(names) <= {f"{w}_{s}" for w in ("w13", "w2") for s in SUFFIXES}
     assert "w2_esp_trellis" in names and "w13_esp_grid" in names
     m.process_weights_after_loading(layer)
-    assert len(layer._esp_experts) == 2 and layer._esp_grouped is None
-    for e, mats in enumerate(layer._esp_experts):
+    assert len(layer.espalier.experts) == 2 and layer.espalier.runner.L is None
+    for e, mats in enumerate(layer.espalier.experts):
         for mt, p in zip(mats, ("gate_proj", "up_proj", "down_proj")):
             assert torch.equal(mt.trellis, want[f"{LM}.0.mlp.experts.{e}.{p}"]["esp_trellis"])
-    assert [(mt.K, mt.cb) for mt in layer._esp_experts[1]] == [(3, 3), (3, 3), (4, 4)]
+    assert [(mt.K, mt.cb) for mt in layer.espalier.experts[1]] == [(3, 3), (3, 3), (4, 4)]
 
 
 def test_moe_method_errors(tmp_path, moe_mod):
@@ -201,5 +201,5 @@ def test_loader_keying_pinned_to_the_reference(moe_mod, lin):
     for shard, want in gold["shard_order"]:
         assert lin.shard_order(tuple(shard) if isinstance(shard, list) else shard) == want, shard
     for name, want in gold["expert_names"].items():
-        m = moe_mod._EXPERT_TENSOR.search(name)
-        assert ([int(m.group(1)), m.group(2), m.group(3)] if m else None) == want, name
+        got = moe_mod.parse_expert_tensor(name)
+        assert (list(got) if got else None) == want, name

@@ -277,34 +277,37 @@ class _Ext:
     # ---- the fused B200 pipeline (no reference counterpart: replaces grouped + epilogues) ----
     @staticmethod
     def moe_gateup(xg, xu, L, uids, ucount, members, slots, P, S, z, counters, xd):
-        check(lib().esp_moe_gateup(xg.data_ptr(), xu.data_ptr(), L.ptr[0].data_ptr(), L.ptr[1].data_ptr(),
-                                   L.k2[0].data_ptr(), L.k2[1].data_ptr(), L.cb[0].data_ptr(), L.cb[1].data_ptr(),
-                                   L.k2_host_gu.data_ptr(), L.cb_host_gu.data_ptr(), L.E, L.svh_g.data_ptr(),
-                                   L.svh_u.data_ptr(), L.suh_d.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
-                                   members.data_ptr(), uids.numel(), members.size(1), slots, P, L.D, L.I, S,
-                                   z.data_ptr(), counters.data_ptr(), xd.data_ptr(), stream_ptr(xg.device)))
+        k2h, cbh = L.host_tables("gu")
+        g, u, d = L.gate, L.up, L.down
+        check(lib().esp_moe_gateup(xg.data_ptr(), xu.data_ptr(), g.ptr.data_ptr(), u.ptr.data_ptr(), g.k2.data_ptr(),
+                                   u.k2.data_ptr(), g.cb.data_ptr(), u.cb.data_ptr(), k2h.data_ptr(), cbh.data_ptr(),
+                                   L.E, g.svh.data_ptr(), u.svh.data_ptr(), d.suh.data_ptr(), uids.data_ptr(),
+                                   ucount.data_ptr(), members.data_ptr(), uids.numel(), members.size(1), slots, P, L.D,
+                                   L.I, S, z.data_ptr(), counters.data_ptr(), xd.data_ptr(), stream_ptr(xg.device)))
 
     @staticmethod
     def moe_layer(xg, xu, L, uids, ucount, members, pick, wts, slots, n_routed, rows, S, z, xd, y, counters, out,
                   out_shared):
-        check(lib().esp_moe_layer(xg.data_ptr(), xu.data_ptr(), L.ptr[0].data_ptr(), L.ptr[1].data_ptr(),
-                                  L.ptr[2].data_ptr(), L.k2[0].data_ptr(), L.k2[1].data_ptr(), L.k2[2].data_ptr(),
-                                  L.cb[0].data_ptr(), L.cb[1].data_ptr(), L.cb[2].data_ptr(), L.k2_host_all.data_ptr(),
-                                  L.cb_host_all.data_ptr(), L.E, L.svh_g.data_ptr(), L.svh_u.data_ptr(),
-                                  L.suh_d.data_ptr(), L.svh_d.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
-                                  members.data_ptr(), uids.numel(), members.size(1), pick.data_ptr(), wts.data_ptr(),
-                                  slots, int(n_routed), rows, L.D, L.I, int(S), z.data_ptr(), xd.data_ptr(),
-                                  y.data_ptr(), counters.data_ptr(), out.data_ptr(), ptr(out_shared), DTYPE[out.dtype],
-                                  stream_ptr(xg.device)))
+        k2h, cbh = L.host_tables("all")
+        g, u, d = L.gate, L.up, L.down
+        check(lib().esp_moe_layer(xg.data_ptr(), xu.data_ptr(), g.ptr.data_ptr(), u.ptr.data_ptr(), d.ptr.data_ptr(),
+                                  g.k2.data_ptr(), u.k2.data_ptr(), d.k2.data_ptr(), g.cb.data_ptr(), u.cb.data_ptr(),
+                                  d.cb.data_ptr(), k2h.data_ptr(), cbh.data_ptr(), L.E, g.svh.data_ptr(),
+                                  u.svh.data_ptr(), d.suh.data_ptr(), d.svh.data_ptr(), uids.data_ptr(),
+                                  ucount.data_ptr(), members.data_ptr(), uids.numel(), members.size(1),
+                                  pick.data_ptr(), wts.data_ptr(), slots, int(n_routed), rows, L.D, L.I, int(S),
+                                  z.data_ptr(), xd.data_ptr(), y.data_ptr(), counters.data_ptr(), out.data_ptr(),
+                                  ptr(out_shared), DTYPE[out.dtype], stream_ptr(xg.device)))
 
     @staticmethod
     def moe_down(xd, L, uids, ucount, members, pick, wts, slots, n_routed, rows, y, counters, out, out_shared):
-        check(lib().esp_moe_down(xd.data_ptr(), L.ptr[2].data_ptr(), L.k2[2].data_ptr(), L.cb[2].data_ptr(),
-                                 L.k2_host_d.data_ptr(), L.cb_host_d.data_ptr(), L.E, L.svh_d.data_ptr(),
-                                 uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), uids.numel(), members.size(1),
-                                 pick.data_ptr(), wts.data_ptr(), slots, int(n_routed), rows, L.I, L.D, y.data_ptr(),
-                                 counters.data_ptr(), out.data_ptr(), ptr(out_shared), DTYPE[out.dtype],
-                                 stream_ptr(xd.device)))
+        k2h, cbh = L.host_tables("d")
+        d = L.down
+        check(lib().esp_moe_down(xd.data_ptr(), d.ptr.data_ptr(), d.k2.data_ptr(), d.cb.data_ptr(), k2h.data_ptr(),
+                                 cbh.data_ptr(), L.E, d.svh.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
+                                 members.data_ptr(), uids.numel(), members.size(1), pick.data_ptr(), wts.data_ptr(),
+                                 slots, int(n_routed), rows, L.I, L.D, y.data_ptr(), counters.data_ptr(),
+                                 out.data_ptr(), ptr(out_shared), DTYPE[out.dtype], stream_ptr(xd.device)))
 
 
 @lru_cache(1)

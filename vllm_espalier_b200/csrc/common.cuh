@@ -1,5 +1,5 @@
 // Shared device helpers of the Espalier B200 kernels: status codes, 16-bit float conversions, the 128-point
-// Walsh-Hadamard transform in the reference's butterfly order, bounded mbarrier waits and bulk (TMA) copies.
+// Walsh-Hadamard transform in the reference's butterfly order, bounded mbarrier waits, 16-byte asynchronous copies.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -90,7 +90,7 @@ __device__ __forceinline__ void fwht128(float (&v)[4], int lane) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// mbarrier + bulk-copy (TMA) primitives, sm_90+ PTX. Waits are bounded: after `limit` polls the wait reports
+// mbarrier primitives, sm_90+ PTX. Waits are bounded: after WAIT_NS of wall time the wait reports
 // ESP_ERR_TIMEOUT and returns false, so no kernel can spin forever.
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

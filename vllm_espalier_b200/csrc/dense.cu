@@ -7,7 +7,7 @@
 //
 // B200 design:
 //   * rot_kernel writes fp16 H(x * suh_s) / sqrt(128) for every matrix once, in a tile-major layout
-//     [s][k-tile][k-half][row][8] whose per-k-tile slice is one contiguous bulk copy (and bank-conflict free as an MMA
+//     [s][k-tile][k-half][row][8] whose per-k-tile slice is one contiguous run of 16-byte copies (and bank-conflict free as an MMA
 //     B fragment).
 //   * dense_kernel: one CTA per SM. The layer is a list of units (128-column block, 16-row k-tile) in block-major
 //     order, split into G contiguous ranges, one per CTA: with fewer blocks than SMs, S = SMs / blocks equal k-slices
@@ -618,23 +618,18 @@ int launch_dense_ntg(const DenseParams& p, bool fused, void* stream) {
 #undef ESP_NTG
 }
 
-}  // namespace
-}  // namespace esp
+// Everything esp_dense checks and derives on the host, before any device work.
+struct DensePlan {
+    DenseParams p;
+    RotParams r;
+    bool fused;
+    int K;
+    int cb;
+};
 
-using namespace esp;
-
-extern "C" {
-
-size_t esp_dense_xh_bytes(int m, int k, int n_mats) {
-    const int mp = (m + 7) / 8 * 8;
-    return (size_t)n_mats * mp * k * 2;
-}
-
-size_t esp_dense_z_bytes(int m) { return (size_t)2 * device_sms() * CTAS_PER_SM * m * 128 * 4; }
-
-int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
-              int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
-              size_t z_bytes, int* counters, int n_counters, void* stream) {
+int dense_plan(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
+               int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
+               size_t z_bytes, int* counters, int n_counters, DensePlan& pl) {
     ESP_REQUIRE(x && y && mats && xh && counters, ESP_ERR_INVALID, "esp_dense: null pointer");
     ESP_REQUIRE(n_mats >= 1 && n_mats <= MAX_SHARDS, ESP_ERR_INVALID, "esp_dense: 1 to 4 matrices a launch");
     ESP_REQUIRE(m >= 1 && m <= 32, ESP_ERR_INVALID, "esp_dense: 1 to 32 rows");
@@ -645,9 +640,12 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
     ESP_REQUIRE(x_stride >= k && aligned(x, 16) && (x_stride * (x_dtype == F32 ? 4 : 2)) % 8 == 0, ESP_ERR_INVALID,
                 "esp_dense: x rows must be 8-byte aligned with a stride >= K");
     const int K = k2 / 2;
-    DenseParams p = {};
+    pl = DensePlan{};
+    pl.K = K;
+    pl.cb = cb;
+    DenseParams& p = pl.p;
+    RotParams& r = pl.r;
     int nbt = 0;
-    RotParams r = {};
     for (int s = 0; s < n_mats; ++s) {
         const esp_matrix_t& mt = mats[s];
         ESP_REQUIRE(mt.trellis && mt.suh && mt.svh, ESP_ERR_INVALID, "esp_dense: matrix %d has a null pointer", s);
@@ -702,12 +700,12 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
     const int max_kt = (int)std::min<long long>(p.KT, per_cta);
     const int chunks = std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
     // up to 8 rows the in-kernel rotation is cheaper than a rotation launch; above, its loads serialise per row
-    const bool fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks) <= SMEM_LIMIT;
+    pl.fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks) <= SMEM_LIMIT;
     p.x = x;
     p.x_dtype = x_dtype;
     p.x_stride = x_stride;
-    p.xh_chunks = fused ? chunks : 0;
-    if (!fused) {
+    p.xh_chunks = pl.fused ? chunks : 0;
+    if (!pl.fused) {
         r.x = x;
         r.x_dtype = x_dtype;
         r.x_stride = x_stride;
@@ -716,19 +714,50 @@ int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, cons
         r.Mp = mp;
         r.K = k;
         r.KT = k / 16;
-        if (int rc = launch(rot_kernel, dim3((k / 128 + 3) / 4, mp, n_mats), dim3(128), 0, stream, true, r)) return rc;
     }
+    return ESP_OK;
+}
 
+int dense_run(const DensePlan& pl, void* stream) {
+    if (!pl.fused) {
+        const RotParams& r = pl.r;
+        if (int rc = launch(rot_kernel, dim3((r.K / 128 + 3) / 4, r.Mp, pl.p.n), dim3(128), 0, stream, true, r))
+            return rc;
+    }
     int rc = ESP_ERR_UNSUPPORTED;
-    switch (cb * 16 + K) {
+    switch (pl.cb * 16 + pl.K) {
 #define ESP_DENSE_CASE(CB_, K_) \
-    case CB_ * 16 + K_: rc = launch_dense_ntg<CB_, K_>(p, fused, stream); break;
+    case CB_ * 16 + K_: rc = launch_dense_ntg<CB_, K_>(pl.p, pl.fused, stream); break;
         ESP_FOR_EACH_CASE(ESP_DENSE_CASE)
 #undef ESP_DENSE_CASE
-        default: return set_error(ESP_ERR_UNSUPPORTED, "esp_dense: unsupported codebook/width: cb=%d k2=%d", cb, k2);
+        default: return set_error(ESP_ERR_UNSUPPORTED, "esp_dense: unsupported codebook/width: cb=%d K=%d", pl.cb, pl.K);
     }
     if (rc) return rc;
     return ok();
+}
+
+}  // namespace
+}  // namespace esp
+
+using namespace esp;
+
+extern "C" {
+
+size_t esp_dense_xh_bytes(int m, int k, int n_mats) {
+    const int mp = (m + 7) / 8 * 8;
+    return (size_t)n_mats * mp * k * 2;
+}
+
+size_t esp_dense_z_bytes(int m) { return (size_t)2 * device_sms() * CTAS_PER_SM * m * 128 * 4; }
+
+int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
+              int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
+              size_t z_bytes, int* counters, int n_counters, void* stream) {
+    DensePlan pl;
+    if (int rc = dense_plan(x, x_dtype, x_stride, m, k, mats, n_mats, k2, cb, y, y_dtype, y_stride, xh, xh_bytes, z,
+                            z_bytes, counters, n_counters, pl))
+        return rc;
+    return dense_run(pl, stream);
 }
 
 int esp_dequant(const int16_t* trellis, int kin, int n, int k2, int cb, uint16_t* out, void* stream) {
@@ -780,7 +809,8 @@ namespace {
 constexpr int NOALLOC_MAX_K = 4096;            // input features
 constexpr int NOALLOC_MAX_BLOCKS = 8192;       // 128-column blocks of all matrices of one call (1,048,576 columns)
 constexpr int NOALLOC_MAX_SMS = 160;
-constexpr size_t NOALLOC_Z = (size_t)2 * NOALLOC_MAX_SMS * 32 * 128 * 4;   // partial sums: 2 a CTA x 32 rows x 128 cols
+// partial sums: 2 slots a CTA (CTAS_PER_SM a streaming multiprocessor) x 32 rows x 128 columns
+constexpr size_t NOALLOC_Z = (size_t)2 * NOALLOC_MAX_SMS * CTAS_PER_SM * 32 * 128 * 4;
 constexpr size_t NOALLOC_XH = (size_t)MAX_SHARDS * 32 * NOALLOC_MAX_K * 2;
 constexpr size_t NOALLOC_CNT = (size_t)NOALLOC_MAX_BLOCKS * 4;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_Z + NOALLOC_XH + NOALLOC_CNT];   // 6.0 MiB
@@ -816,12 +846,12 @@ extern "C" int esp_dense_noalloc(const void* x, int x_dtype, long long x_stride,
                                  long long y_stride, void* stream) {
     using namespace esp;
     ESP_REQUIRE(mats && n_mats >= 1 && n_mats <= MAX_SHARDS, ESP_ERR_INVALID, "esp_dense_noalloc: 1 to 4 matrices");
-    int nbt = 0;
-    for (int s = 0; s < n_mats; ++s) nbt += mats[s].n / 128;
+    long long cols = 0;
+    for (int s = 0; s < n_mats; ++s) cols += mats[s].n;
     ESP_REQUIRE(k <= NOALLOC_MAX_K, ESP_ERR_INVALID,
                 "esp_dense_noalloc: K=%d exceeds the static scratch limit of %d inputs", k, NOALLOC_MAX_K);
-    ESP_REQUIRE(nbt <= NOALLOC_MAX_BLOCKS, ESP_ERR_INVALID,
-                "esp_dense_noalloc: %d output columns exceed the static scratch limit of %d", nbt * 128,
+    ESP_REQUIRE(cols <= (long long)NOALLOC_MAX_BLOCKS * 128, ESP_ERR_INVALID,
+                "esp_dense_noalloc: %lld output columns exceed the static scratch limit of %d", cols,
                 NOALLOC_MAX_BLOCKS * 128);
     ESP_REQUIRE(device_sms() <= NOALLOC_MAX_SMS, ESP_ERR_INVALID,
                 "esp_dense_noalloc: %d SMs exceed the static scratch limit of %d", device_sms(), NOALLOC_MAX_SMS);
@@ -830,9 +860,13 @@ extern "C" int esp_dense_noalloc(const void* x, int x_dtype, long long x_stride,
     float* z = reinterpret_cast<float*>(base);
     void* xh = base + NOALLOC_Z;
     int* counters = reinterpret_cast<int*>(base + NOALLOC_Z + NOALLOC_XH);
+    // every argument is checked before the shared array is touched: a rejected call leaves it as it was
+    DensePlan pl;
+    if (int rc = dense_plan(x, x_dtype, x_stride, m, k, mats, n_mats, k2, cb, y, y_dtype, y_stride, xh, NOALLOC_XH, z,
+                            NOALLOC_Z, counters, NOALLOC_MAX_BLOCKS, pl))
+        return rc;
     // the counters must start at zero; a call that completes leaves them zero, this also covers one that did not
-    const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)std::max(nbt, 1) * 4, static_cast<cudaStream_t>(stream));
+    const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)pl.p.NB * 4, static_cast<cudaStream_t>(stream));
     ESP_REQUIRE(e == cudaSuccess, ESP_ERR_CUDA, "esp_dense_noalloc: clearing counters: %s", cudaGetErrorString(e));
-    return esp_dense(x, x_dtype, x_stride, m, k, mats, n_mats, k2, cb, y, y_dtype, y_stride, xh, NOALLOC_XH, z,
-                     NOALLOC_Z, counters, NOALLOC_MAX_BLOCKS, stream);
+    return dense_run(pl, stream);
 }

@@ -6,7 +6,7 @@
 // (input k) 2t + 8((j >> 1) & 1) + (j & 1) and column (output n) g + 8(j >> 2) of the tile, lane = 4g + t.
 //
 // Design (B200): a lane reads the 2-3 words that hold its eight windows straight from shared memory (the tile was
-// brought in by a bulk copy), aligns them once with a funnel shift and cuts the eight states with constant shifts.
+// staged there by the producer warps' asynchronous copies), aligns them once with a funnel shift and cuts the eight states with constant shifts.
 // The eight values are exactly the lane's A fragment of an m16n8k16 MMA whose M dimension is the tile's 16 output
 // columns and whose N dimension is 8 tokens (weights as A: one MMA per tile per 8 tokens, no register shuffles).
 //

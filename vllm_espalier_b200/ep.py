@@ -136,7 +136,7 @@ class EPLayer:
         lpf = lp.reshape(-1)
         stride = recv_x.stride(1)                 # rows of the packed dispatch buffer: D values, then the picks
         e.group(lpf, self.ids, self.count, self.members, rows, slots, self.nl + 1)
-        e.rot_in(recv_x, stride, lpf, L.suh_g, L.suh_u, self.xg, self.xu, rows, D, slots, self.nl + 1)
+        e.rot_in(recv_x, stride, lpf, L.gate.suh, L.up.suh, self.xg, self.xu, rows, D, slots, self.nl + 1)
         e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, P, self.S, self.z, self.cnt_gu,
                      self.xd)
         e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
