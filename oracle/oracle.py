@@ -281,7 +281,7 @@ def moe(x: np.ndarray, pick: np.ndarray, wts: np.ndarray, experts, n_routed: int
         key = (e, which)
         if key not in cache:
             T, K, cb = experts[e][which][:3]
-            cache[key] = dequant(T, K, cb).astype(np.float32)
+            cache[key] = dequant_f32(T, K, cb)      # the same values as dequant's, through the faster decode
         return cache[key]
 
     y = np.zeros((R, slots, D), np.float32)

@@ -84,6 +84,8 @@ class _Ref:
         k = 8
         pick, wts, _ = O.route(hb, gb, k, sgb, L.shared_id)
         self.picks.append(torch.from_numpy(pick).to(self.dev))
+        self.routes.append((torch.from_numpy(np.ascontiguousarray(pick[:, :k])).to(self.dev),
+                            torch.from_numpy(np.ascontiguousarray(wts[:, :k])).to(self.dev)))
         ys = {}
         for e in np.unique(pick):
             rows, slots = np.nonzero(pick == e)
@@ -106,7 +108,7 @@ class _Ref:
     def forward(self, tokens):
         import bench as B
         m = self.m
-        self.picks = []
+        self.picks, self.routes = [], []
         x = m.embed[tokens]
         for blk, layer in zip(m.blocks, m.moe):
             h = B.rmsnorm(x, blk["n1"])
@@ -151,3 +153,28 @@ def test_full_decoder_top1_agreement(dev):
           f"another fp32 order {agree_alt}/{total} = {frac_alt:.4f}; rows routed alike by layer (this library / other "
           f"order): first {alike[0]:.3f} / {alike_alt[0]:.3f}, mean {alike.mean():.3f} / {alike_alt.mean():.3f}")
     assert frac >= frac_alt - 0.03, f"top-1 agreement {frac:.4f} vs the reference's own order floor {frac_alt:.4f}"
+
+
+FORCED_STEPS = 16          # 512 rows: 99.7% allows one disagreement
+
+
+def test_forced_routing_top1_agreement(dev):
+    """The arithmetic alone: every layer of this library's decoder is fed the reference side's routing (its exact
+    picks and renormalised weights, from the CPU oracle on the reference's own hidden state), so no row can follow
+    another expert, and the dense, expert and head arithmetic must give the reference's top-1 token on at least 99.7%
+    of rows."""
+    import bench as B
+    model = B.Decoder(dev)
+    ref = _Ref(model, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    agree = total = 0
+    for _ in range(FORCED_STEPS):
+        tokens = torch.randint(0, B.VOCAB, (ROWS,), device=dev, generator=g)
+        want = ref.forward(tokens)
+        ours = model.forward(tokens, forced=ref.routes).float()
+        agree += int((ours.argmax(1) == want.argmax(1)).sum())
+        total += ROWS
+    frac = agree / total
+    print(f"forced-routing top-1 agreement with the reference: {agree}/{total} = {frac:.4f}")
+    assert frac >= 0.997, f"top-1 agreement {frac:.4f} with both sides on the same routing"

@@ -96,6 +96,18 @@ def test_config2_block_vs_oracle(dev, M):
         assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
 
 
+@pytest.mark.parametrize("M", [1, 8, 32])
+def test_config1_layer_vs_oracle(dev, M):
+    """BASELINE config 1's exact shape: one 2048 -> 4096 matrix, 4-bit trellis, int6 codebook (kernel codebook 7)."""
+    ms, x, ref = _layer("cfg1", 2048, [4096], 7, 8, M, "bf16", dev)
+    y = D.Dense(ms).forward(x)
+    torch.cuda.synchronize()
+    e, fl = rel_err(f32(y), ref), floor_err(ref, y.dtype)
+    assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
+    assert _lib.device_status() == 0
+    assert int(D.workspace(dev).counters.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("M", [1, 17])
 def test_wide_layer_vs_oracle(dev, M):
     """A layer with more 128-column blocks (240) than SMs: one range an SM over whole blocks with a partial block at

@@ -4,6 +4,8 @@ fused 4-launch pipeline (routed2) and the reference-kernel sequence (routed), ro
 (the reference's tests/gpu_route.py, gpu_grouped.py, gpu_grouped_shared.py gates, on synthetic data)."""
 from __future__ import annotations
 
+import functools
+
 import numpy as np
 import pytest
 import torch
@@ -258,6 +260,7 @@ def test_empty_calls_return_ok(dev):
     assert lib.esp_ep_combine(16, 16, 16, 16, null, 1, 0, 2048, 9, 8, 256, 2, 0, null) == 0
 
 
+@functools.lru_cache(maxsize=2)
 def _config3_layer(dev, seed=0):
     """256 routed experts 2048 -> 512 -> 2048 with widths 1/2/3 bits (p = .3/.5/.2; 1-2 bit E2M1,
     3 bit int5) and one 4-bit int6 shared expert; router bf16 [256, 2048] N(0, 1/sqrt(2048)); shared gate [2048]."""
@@ -279,7 +282,7 @@ def _config3_layer(dev, seed=0):
     return ex_np, gate, sgate
 
 
-@pytest.mark.parametrize("R", [1, 3])
+@pytest.mark.parametrize("R", [1, 3, 8, 32])
 def test_config3_layer_with_fused_routing(dev, R):
     ex_np, gate_b, sgate_b = _config3_layer(dev)
     mats = build(ex_np, dev)
@@ -299,6 +302,8 @@ def test_config3_layer_with_fused_routing(dev, R):
         e = rel_err(f32(got), want)
         fl = rel_err(C.bf16_to_f32(C.bf16_bits(want)), want)
         assert e < 1e-2 and e < fl + 2e-3, f"max rel err {e:.3e} (floor {fl:.3e})"
+    assert _lib.device_status() == 0
+    assert int(s.cnt_layer.abs().sum()) == 0
 
 
 @pytest.mark.parametrize("R", [1, 5, 32])
