@@ -134,6 +134,21 @@ def test_int6_single_fma_constant_exhaustive():
     assert np.array_equal(q, O.codebook_table(23).view(np.float16).astype(np.float64))
 
 
+@pytest.mark.parametrize("cb,idx,c_hi,c_lo", [(6, 22, 0x3436, 0x0666), (7, 23, 0x3014, 0x8319)])
+def test_int_weight_two_term_exhaustive(cb, idx, c_hi, c_lo):
+    """int_weight2 (trellis.cuh), the GEMVs' int5 / int6 weights: w = fl16(q c_hi + fl16(q c_lo)) from the index q
+    (one fp16 multiply, one fp16 fused multiply-add) equals the reference's fl16(fl32(q c)) for every state, up to the
+    sign of zero. The fp16 products are emulated exactly in float64 and rounded once."""
+    q = O.codebook_table(idx).view(np.float16).astype(np.float64)
+    hi, lo = (np.array([v], np.uint16).view(np.float16).astype(np.float64)[0] for v in (c_hi, c_lo))
+    c = np.float32(3.94921875) / np.float32(15.0 if cb == 6 else 31.0)
+    assert hi == np.float64(np.float16(c)) and lo == np.float64(np.float16(np.float64(c) - hi))
+    r = (q * lo).astype(np.float16).astype(np.float64)        # HMUL2: the exact product rounded to fp16
+    w = (q * hi + r).astype(np.float16)                        # HFMA2: exact q * c_hi + r, rounded once
+    want = O.codebook_table(cb).view(np.float16)
+    assert np.array_equal(w.astype(np.float32), want.astype(np.float32))
+
+
 def test_int_grid_value_from_index():
     """c * q in fp32 rounded to fp16 (the exact form) for every state."""
     for cb, idx in ((6, 22), (7, 23)):

@@ -194,7 +194,7 @@ __device__ __forceinline__ void rotate_items(const DenseParams& p, const __half*
 }
 
 template <int CB, int K, int NTG, bool FUSED>
-__global__ void __launch_bounds__(THREADS, 1) dense_kernel(const __grid_constant__ DenseParams p) {
+__global__ void __launch_bounds__(THREADS, CTAS_PER_SM) dense_kernel(const __grid_constant__ DenseParams p) {
     constexpr int TW = 8 * K;                          // words a tile
     constexpr int UNIT_W = 8 * TW;                     // words a unit (8 tiles)
     constexpr int MP = 8 * NTG;

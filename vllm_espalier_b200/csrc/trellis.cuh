@@ -12,9 +12,11 @@
 //
 // Codebooks (kernel ids of the reference, experts_grouped.cuh:23-80): 1 mcg, 3 E2M1, 6 int5, 7 int6.
 //   exact form  (cb_exact): the reference's fp16 values bit for bit (dequant, tests).
-//   kernel form (cb_gemv):  the same values divided by a per-codebook step, exact in fp16, for the GEMVs:
-//                           E2M1 as multiples of C = 0.75 (hardware e2m1 conversion), int5 / int6 as the integer grid
-//                           index q; the GEMV epilogue multiplies its fp32 sums by the step (cb_step).
+//   kernel form (cb_gemv):  what the GEMVs multiply by. mcg, int5 and int6: the exact values themselves, so every
+//                           product uses a weight bit-identical to the reference's decode; E2M1: the exact values
+//                           divided by C = 0.75 (hardware e2m1 conversion; multiples of C are exact in fp16, so the
+//                           sum times C equals the sum of the exact products). The GEMV epilogue multiplies its fp32
+//                           sums by cb_step: C for E2M1, 1 otherwise.
 #pragma once
 
 #include "common.cuh"
@@ -44,9 +46,37 @@ __device__ __forceinline__ uint32_t mcg2(uint32_t s0, uint32_t s1) {
 constexpr float E2M1_C = 0.75f;
 constexpr float E2M1_INV_C = 0x1.55554p+0f;   // fl32(fl32(1 / 0.75) * fl32(1 - 2^-20))
 
+// Two fp32 lanes in one 64-bit register for the sm_100 packed fp32 instructions (each lane an IEEE round-to-nearest
+// operation of its own, the same results as two scalar instructions in half the issue slots).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2splat(float a) { return f2pack(a, a); }
+
 __device__ __forceinline__ uint32_t e2m1_units2(uint32_t v) {
     const float2 f = __half22float2(u2h(v));
-    const float a = __fmul_rn(f.x, E2M1_INV_C), b = __fmul_rn(f.y, E2M1_INV_C);
+    float a, b;
+    f2unpack(mul_f32x2(f2pack(f.x, f.y), f2splat(E2M1_INV_C)), a, b);
     uint32_t h;
     // a -> low half, b -> high half: the packing puts the first source in the upper nibble
     asm("{ .reg .b8 t; cvt.rn.satfinite.e2m1x2.f32 t, %1, %2; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(h) : "f"(b), "f"(a));
@@ -68,32 +98,43 @@ constexpr float INT6_K_FMA = 0x1.f660bcp+2f;   // INT6_K + 1 ulp
 template <int CB>
 __device__ __forceinline__ uint32_t int_index2(uint32_t v) {
     const float2 f = __half22float2(u2h(v));
-    uint32_t a, b;
-    if constexpr (CB == 7) {
-        a = __float_as_uint(__fmaf_rn(f.x, INT6_K_FMA, INT_MAGIC));
-        b = __float_as_uint(__fmaf_rn(f.y, INT6_K_FMA, INT_MAGIC));
-    } else {
-        a = __float_as_uint(__fadd_rn(__fmul_rn(f.x, INT5_K), INT_MAGIC));
-        b = __float_as_uint(__fadd_rn(__fmul_rn(f.y, INT5_K), INT_MAGIC));
-    }
-    const __half2 q = u2h(__byte_perm(a, b, 0x5410));
+    const uint64_t fv = f2pack(f.x, f.y);
+    uint64_t r;
+    if constexpr (CB == 7) r = fma_f32x2(fv, f2splat(INT6_K_FMA), f2splat(INT_MAGIC));
+    else r = add_f32x2(mul_f32x2(fv, f2splat(INT5_K)), f2splat(INT_MAGIC));
+    float a, b;
+    f2unpack(r, a, b);
+    const __half2 q = u2h(__byte_perm(__float_as_uint(a), __float_as_uint(b), 0x5410));
     return h2u(__hsub2(q, __float2half2_rn(1056.0f)));
 }
 
-// per-codebook factor the kernel form is multiplied by (the reference's c = 3.94921875f / 15 or / 31 in fp32)
-__host__ __device__ __forceinline__ float cb_step(int cb) {
-    return cb == 3 ? E2M1_C : cb == 6 ? 3.94921875f / 15.0f : cb == 7 ? 3.94921875f / 31.0f : 1.0f;
+// int5 / int6 weights w = fl16(fl32(q * c)), c = fl32(3.94921875 / 15 or / 31) (experts_grouped.cuh:39-55), from the
+// grid index q in fp16 by two fp16 operations: w = fl16(q * c_hi + fl16(q * c_lo)) with c_hi = fl16(c) and
+// c_lo = fl16(c - c_hi). For every index |q| <= 31 this is the reference's value bit for bit (checked exhaustively;
+// no single fp16 factor reproduces all of them). int6's c_lo is an fp16 subnormal, which fp16 arithmetic keeps.
+constexpr uint32_t INT5_C_HI2 = 0x34363436u, INT5_C_LO2 = 0x06660666u;
+constexpr uint32_t INT6_C_HI2 = 0x30143014u, INT6_C_LO2 = 0x83198319u;
+
+template <int CB>
+__device__ __forceinline__ uint32_t int_weight2(uint32_t v) {
+    const __half2 q = u2h(int_index2<CB>(v));
+    const __half2 hi = u2h(CB == 6 ? INT5_C_HI2 : INT6_C_HI2), lo = u2h(CB == 6 ? INT5_C_LO2 : INT6_C_LO2);
+    return h2u(__hfma2(q, hi, __hmul2(q, lo)));
 }
+
+// factor the fp32 sums of kernel-form products are multiplied by: C for E2M1 (values in units of C), 1 otherwise
+__host__ __device__ __forceinline__ float cb_step(int cb) { return cb == 3 ? E2M1_C : 1.0f; }
 
 template <int CB>
 __device__ __forceinline__ uint32_t cb_gemv(uint32_t s0, uint32_t s1) {
     const uint32_t m = mcg2(s0, s1);
     if constexpr (CB == 1) return m;
     else if constexpr (CB == 3) return e2m1_units2(m);
-    else return int_index2<CB>(m);
+    else return int_weight2<CB>(m);
 }
 
-// the reference's fp16 values bit for bit
+// the reference's fp16 values bit for bit. int5 / int6 through rintf, which keeps the sign of a zero index (the
+// magic add of int_index2 gives +0 where rintf gives -0; the sign of a zero weight changes no GEMV sum)
 template <int CB>
 __device__ __forceinline__ uint32_t cb_exact(uint32_t s0, uint32_t s1) {
     const uint32_t m = mcg2(s0, s1);
