@@ -66,8 +66,8 @@ def test_dense_op_windows_equal_rows(dev):
 def test_gemm_prefill_branch(dev, monkeypatch):
     ms, xf, ref = _mats("op-gemm", 512, [256], 7, 8, 64, dev)
     m = ms[0]
-    monkeypatch.setattr(ops, "PREFILL", "gemm")
-    y = ops._matmul(torch.from_numpy(xf).to(dev).half(), m.trellis, m.suh, m.svh, m.K, m.cb)
+    monkeypatch.setattr(ops, "PREFILL", "gemm")            # 64 rows > 32: the op takes the gemm branch
+    y = torch.ops.espalier.matmul(torch.from_numpy(xf).to(dev).half(), m.trellis, m.suh, m.svh, m.K, m.cb)
     torch.cuda.synchronize()
     assert y.shape == (64, 256)
     assert rel_err(f32(y), ref) < 1e-2       # cuBLAS fp16 output: the fp16 floor, not a bit pattern

@@ -83,6 +83,7 @@ struct DenseParams {
     int NB;                      // 128-column blocks
     int S;                       // > 1: the S CTAs of a block form a thread-block cluster (block-aligned k-slices)
     float scale;                 // codebook step of the kernel form
+    int npre;                    // fused path: units decoded ahead of the launch wait (whole stages, one segment)
 };
 
 struct RotParams {
@@ -203,7 +204,8 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) dense_kernel(const __gri
     extern __shared__ __align__(128) uint32_t smem[];
     float* red = reinterpret_cast<float*>(smem + (size_t)STAGES * STAGE_W);   // [MP][RED_STRIDE]
     uint32_t* xrot = reinterpret_cast<uint32_t*>(red + MP * RED_STRIDE);      // fused: [chunks][8][2][MP][4]
-    uint64_t* full = reinterpret_cast<uint64_t*>(xrot + (FUSED ? (size_t)p.xh_chunks * 8 * SLICE_W : 0));
+    uint4* pre = reinterpret_cast<uint4*>(xrot + (FUSED ? (size_t)p.xh_chunks * 8 * SLICE_W : 0));  // [npre][8][32]
+    uint64_t* full = reinterpret_cast<uint64_t*>(pre + (FUSED ? (size_t)p.npre * 8 * 32 : 0));
     uint64_t* empty = full + STAGES;
     __shared__ int s_lastv[2];
 
@@ -301,7 +303,6 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) dense_kernel(const __gri
     } else {
 
         // ---------- consumers: warp w decodes tile w of every unit; even and odd units into separate sums ----------
-        pdl_wait();
         const int g = lane >> 2, t = lane & 3;
         const int grp = warp >> 3, wl = warp & 7;
         constexpr int CT = CWARPS * 32;
@@ -322,15 +323,59 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) dense_kernel(const __gri
         bool from_zero = kt0 == 0;     // the current segment starts at the block's first k-tile
         int chunk0 = 0;                // fused: first 128-input chunk held in xrot
         bool seg_start = true;
-        while (li < n) {
-            if (FUSED && seg_start) {      // rotate this segment's inputs into shared memory
-                const int seg_kt1 = min(p.KT, kt + (n - li));
-                chunk0 = kt >> 3;
-                const int nch = ((seg_kt1 + 7) >> 3) - chunk0;
-                rotate_items<MP>(p, p.s[shard_of(bg, p)].suh, chunk0, nch, warp, lane, reinterpret_cast<__half*>(xrot));
-                named_sync(1, CT);
-                seg_start = false;
+        auto rotate_segment = [&]() {  // rotate the current segment's inputs (from unit li on) into shared memory
+            const int seg_kt1 = min(p.KT, kt + (n - li));
+            chunk0 = kt >> 3;
+            const int nch = ((seg_kt1 + 7) >> 3) - chunk0;
+            rotate_items<MP>(p, p.s[shard_of(bg, p)].suh, chunk0, nch, warp, lane, reinterpret_cast<__half*>(xrot));
+            named_sync(1, CT);
+            seg_start = false;
+        };
+        if constexpr (FUSED) {
+            // Decode ahead: the weights are not the previous kernel's output, so the first npre units (whole stages
+            // of this CTA's one segment) are decoded into shared memory before the wait on that kernel, while this
+            // CTA would otherwise sit idle; their products follow the wait in the loop's own order and accumulators,
+            // so the sums are the bits the loop would give.
+            for (int sidx = 0; sidx < p.npre / UPS; ++sidx) {
+                mbar_wait(&full[slot], phase);
+                const uint32_t* st = smem + (size_t)slot * STAGE_W;
+    #pragma unroll
+                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                    const int jj = j2 * GROUPS + grp;
+                    uint32_t a[4];
+                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                    pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane] = make_uint4(a[0], a[1], a[2], a[3]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (++slot == STAGES) {
+                    slot = 0;
+                    phase ^= 1;
+                }
             }
+        }
+        pdl_wait();
+        if constexpr (FUSED) {
+            if (p.npre) {
+                rotate_segment();
+                for (int sidx = 0; sidx < p.npre / UPS; ++sidx) {
+    #pragma unroll
+                    for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                        const int jj = j2 * GROUPS + grp;
+                        const uint4 v = pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane];
+                        const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+                        const uint32_t* xs = xrot + (size_t)(kt + sidx * UPS + jj - 8 * chunk0) * SLICE_W;
+    #pragma unroll
+                        for (int q = 0; q < NTG; ++q)
+                            mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                    }
+                }
+                kt += p.npre;
+                li = p.npre;
+            }
+        }
+        while (li < n) {
+            if (FUSED && seg_start) rotate_segment();   // rotate this segment's inputs into shared memory
             if (j == 0) mbar_wait(&full[slot], phase);
             const uint32_t* st = smem + (size_t)slot * STAGE_W;
             const int stage_n = min(UPS, n - (li - j));
@@ -543,13 +588,22 @@ __global__ void __launch_bounds__(128) had_kernel(const __half* __restrict__ x, 
     store4(y, F16, i, v);
 }
 
-size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks) {
+size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks, int npre) {
     const int tw = 8 * K, unit_w = 8 * tw, slice_w = 8 * ntg * 8;
     return (size_t)STAGES * UPS * (unit_w + (fused ? 0 : slice_w)) * 4 + (size_t)8 * ntg * RED_STRIDE * 4 +
-           (fused ? (size_t)chunks * 8 * slice_w * 4 : 0) + 2 * STAGES * 8;
+           (fused ? (size_t)chunks * 8 * slice_w * 4 + (size_t)npre * 8 * 32 * 16 : 0) + 2 * STAGES * 8;
 }
 
-constexpr size_t SMEM_LIMIT = 200 * 1024;
+constexpr size_t SMEM_LIMIT = 220 * 1024;
+
+// ESPALIER_DENSE_AHEAD=0 turns the decode ahead of the launch wait off (for comparison); on by default.
+bool ahead_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("ESPALIER_DENSE_AHEAD");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 
 // ESPALIER_DENSE_CLUSTER=1 finishes split blocks inside a thread-block cluster (DSMEM reads of the k-slices' partials)
 // instead of through global partials. Off by default: on the config-2 block it measured slower (1.09 vs 0.84 ms for
@@ -566,7 +620,7 @@ bool cluster_enabled() {
 template <int CB, int K, int NTG, bool FUSED>
 int launch_dense(DenseParams p, void* stream) {
     auto kern = dense_kernel<CB, K, NTG, FUSED>;
-    const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks);
+    const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks, FUSED ? p.npre : 0);
     static size_t opted = 0;
     if (smem > opted) {
         if (int rc = allow_smem(kern, FUSED ? SMEM_LIMIT : smem)) return rc;
@@ -700,7 +754,15 @@ int dense_plan(const void* x, int x_dtype, long long x_stride, int m, int k, con
     const int max_kt = (int)std::min<long long>(p.KT, per_cta);
     const int chunks = std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
     // up to 8 rows the in-kernel rotation is cheaper than a rotation launch; above, its loads serialise per row
-    pl.fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks) <= SMEM_LIMIT;
+    pl.fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks, 0) <= SMEM_LIMIT;
+    // decode ahead (fused path, one segment a CTA, i.e. fewer blocks than CTAs): as many whole stages as the shared
+    // memory beside the ring holds, leaving the loop at least one unit of every CTA (U / G is the smallest range)
+    p.npre = 0;
+    if (pl.fused && ahead_enabled() && nbt < device_sms() * CTAS_PER_SM) {
+        const size_t base = dense_smem_bytes(K, 1, true, chunks, 0);
+        const int cap = base < SMEM_LIMIT ? (int)((SMEM_LIMIT - base) / (8 * 32 * 16)) : 0;
+        p.npre = std::max(0, std::min(cap, p.U / p.G - 1) / UPS * UPS);
+    }
     p.x = x;
     p.x_dtype = x_dtype;
     p.x_stride = x_stride;

@@ -61,11 +61,6 @@ __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
-__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
 __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
     uint64_t r;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
@@ -95,16 +90,23 @@ constexpr float INT_MAGIC = 12608544.0f;   // 1.5 * 2^23 + 0x6420
 // int5 has no such k' (the feasible interval of k is a single point), so it keeps the product's own rounding.
 constexpr float INT6_K_FMA = 0x1.f660bcp+2f;   // INT6_K + 1 ulp
 
+// int6 uses one packed fp32x2 FMA. int5 keeps scalar multiply and add: the packed multiply followed by the packed add
+// decoded 19 of the 65536 states one index off on a B200 (the result of a single rounding of v k + M, which int5
+// cannot tolerate), the scalar pair none (all states checked on the GPU).
 template <int CB>
 __device__ __forceinline__ uint32_t int_index2(uint32_t v) {
     const float2 f = __half22float2(u2h(v));
-    const uint64_t fv = f2pack(f.x, f.y);
-    uint64_t r;
-    if constexpr (CB == 7) r = fma_f32x2(fv, f2splat(INT6_K_FMA), f2splat(INT_MAGIC));
-    else r = add_f32x2(mul_f32x2(fv, f2splat(INT5_K)), f2splat(INT_MAGIC));
-    float a, b;
-    f2unpack(r, a, b);
-    const __half2 q = u2h(__byte_perm(__float_as_uint(a), __float_as_uint(b), 0x5410));
+    uint32_t a, b;
+    if constexpr (CB == 7) {
+        float fa, fb;
+        f2unpack(fma_f32x2(f2pack(f.x, f.y), f2splat(INT6_K_FMA), f2splat(INT_MAGIC)), fa, fb);
+        a = __float_as_uint(fa);
+        b = __float_as_uint(fb);
+    } else {
+        a = __float_as_uint(__fadd_rn(__fmul_rn(f.x, INT5_K), INT_MAGIC));
+        b = __float_as_uint(__fadd_rn(__fmul_rn(f.y, INT5_K), INT_MAGIC));
+    }
+    const __half2 q = u2h(__byte_perm(a, b, 0x5410));
     return h2u(__hsub2(q, __float2half2_rn(1056.0f)));
 }
 
