@@ -596,26 +596,36 @@ class Decoder:
     def head_bytes(self) -> int:
         return mat_bytes(self.head.mats[0])
 
+    def layer(self, i: int, x: torch.Tensor, forced=None, picks: list | None = None):
+        """Decoder layer i on the residual stream x [R, 2048] bf16 -> (the stream after it, the o projection's output,
+        the routed experts' sum, the gated shared expert's output). `forced` = (pick int32 [R, 8], weights fp32
+        [R, 8]) replaces the layer's own routing; `picks` collects the routing (pick table with the shared slot)."""
+        G, s = self.G, self.s
+        blk, (L, gate, _, _) = self.blocks[i], self.moe[i]
+        R = x.shape[0]
+        h = rmsnorm(x, blk["n1"])
+        attn = blk["o"].forward(mixer_core(blk["qkv"].forward(h), blk["attention"]))
+        x = residual(x, attn)
+        h = rmsnorm(x, blk["n2"])
+        if forced is not None:
+            out, sh = G.routed2(h, forced[0], forced[1], L, s)
+        else:
+            G.route(h, gate, MOE_K, L, s)
+            out, sh = G.routed2(h, None, None, L, s, k=MOE_K)
+        if picks is not None:
+            picks.append(s.pick[:R * (MOE_K + 1)].view(R, MOE_K + 1).clone())
+        return residual(x, out, sh), attn, out, sh
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        return self.head.forward(rmsnorm(x, self.final))
+
     def forward(self, tokens: torch.Tensor, picks: list | None = None, forced: list | None = None) -> torch.Tensor:
         """tokens int64 [R] -> logits bf16 [R, VOCAB] (one decode step). `picks` collects each layer's routing;
-        `forced` = [(pick int32 [R, 8], weights fp32 [R, 8])] a layer replaces the layer's own routing."""
-        G, s = self.G, self.s
+        `forced` = [(pick, weights)] a layer replaces the layers' own routing."""
         x = self.embed[tokens]
-        R = tokens.shape[0]
-        for i, (blk, (L, gate, _, _)) in enumerate(zip(self.blocks, self.moe)):
-            h = rmsnorm(x, blk["n1"])
-            core = mixer_core(blk["qkv"].forward(h), blk["attention"])
-            x = residual(x, blk["o"].forward(core))
-            h = rmsnorm(x, blk["n2"])
-            if forced is not None:
-                out, sh = G.routed2(h, forced[i][0], forced[i][1], L, s)
-            else:
-                G.route(h, gate, MOE_K, L, s)
-                out, sh = G.routed2(h, None, None, L, s, k=MOE_K)
-            if picks is not None:
-                picks.append(s.pick[:R * (MOE_K + 1)].view(R, MOE_K + 1).clone())
-            x = residual(x, out, sh)
-        return self.head.forward(rmsnorm(x, self.final))
+        for i in range(len(self.blocks)):
+            x = self.layer(i, x, None if forced is None else forced[i], picks)[0]
+        return self.logits(x)
 
 
 class DecoderStep(Graphed):
