@@ -125,11 +125,13 @@ class _Ref:
         return B.residual(x, out, sh), attn, out, sh, pick, route
 
     def logits(self, x):
+        """bf16 logits, as the model's head returns them (top-1 then compares the same rounding on both sides, ties
+        to the first index)."""
         import bench as B
         head = self.m.head.mats[0]
         hf = B.rmsnorm(x, self.m.final)
         xh = self.had(hf.float() * head.suh.float()).half().float()
-        return self.had(self.mm(xh, self.W(head, keep=False))) * head.svh.float()
+        return (self.had(self.mm(xh, self.W(head, keep=False))) * head.svh.float()).to(torch.bfloat16)
 
     def forward(self, tokens, forced=None):
         """Records per layer: its input (self.inputs), its outputs (self.outs: o projection, routed, shared), its
@@ -171,7 +173,7 @@ def test_layerwise_parity_and_head_top1(dev, model):
             _, attn, out, sh = model.layer(i, ref.inputs[i], forced=ref.routes[i])
             for got, exp in zip((attn, out, sh), ref.outs[i]):
                 worst = max(worst, rel_err(f32(got), f32(exp)))
-        ours = model.logits(ref.final).float()
+        ours = model.logits(ref.final)
         agree += int((ours.argmax(1) == want.argmax(1)).sum())
         total += ROWS
     frac = agree / total
@@ -193,7 +195,7 @@ def test_forced_routing_reaches_the_fp32_order_floor(dev, model):
         tokens = _tokens(g, dev)
         want = ref.forward(tokens)
         other = alt.forward(tokens, forced=ref.routes)
-        ours = model.forward(tokens, forced=ref.routes).float()
+        ours = model.forward(tokens, forced=ref.routes)
         agree += int((ours.argmax(1) == want.argmax(1)).sum())
         agree_alt += int((other.argmax(1) == want.argmax(1)).sum())
         total += ROWS
@@ -216,7 +218,7 @@ def test_full_decoder_top1_agreement(dev, model):
     for _ in range(STEPS):
         tokens = _tokens(g, dev)
         picks = []
-        ours = model.forward(tokens, picks).float()
+        ours = model.forward(tokens, picks)
         want = ref.forward(tokens)
         other = alt.forward(tokens)
         agree += int((ours.argmax(1) == want.argmax(1)).sum())

@@ -594,7 +594,8 @@ size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks, int npre) {
            (fused ? (size_t)chunks * 8 * slice_w * 4 + (size_t)npre * 8 * 32 * 16 : 0) + 2 * STAGES * 8;
 }
 
-constexpr size_t SMEM_LIMIT = 220 * 1024;
+// dynamic shared memory a CTA may take: most of an SM's 227 KB with one CTA an SM, half of it with two
+constexpr size_t SMEM_LIMIT = (CTAS_PER_SM == 1 ? 220 : 110) * 1024;
 
 // ESPALIER_DENSE_AHEAD=0 turns the decode ahead of the launch wait off (for comparison); on by default.
 bool ahead_enabled() {
