@@ -55,7 +55,14 @@ constexpr int RED_STRIDE = 132;                // fp32 row stride of the reducti
 #ifndef ESP_DENSE_CTAS_PER_SM
 #define ESP_DENSE_CTAS_PER_SM 1
 #endif
-constexpr int CTAS_PER_SM = ESP_DENSE_CTAS_PER_SM;   // persistent CTAs a streaming multiprocessor
+constexpr int CTAS_PER_SM = ESP_DENSE_CTAS_PER_SM;   // CTAs a launch puts on a streaming multiprocessor
+#ifndef ESP_DENSE_RESIDENT
+#define ESP_DENSE_RESIDENT ESP_DENSE_CTAS_PER_SM
+#endif
+// CTAs the resources of one are sized for on a streaming multiprocessor (registers, shared memory): more than
+// CTAS_PER_SM lets the next launch's CTAs become resident beside this one's and decode ahead while it runs
+constexpr int RESIDENT = ESP_DENSE_RESIDENT;
+static_assert(RESIDENT >= CTAS_PER_SM, "a launch's CTAs must fit");
 
 struct DShard {
     const uint32_t* T;   // trellis words [K/16][N/16][8K]
@@ -195,7 +202,7 @@ __device__ __forceinline__ void rotate_items(const DenseParams& p, const __half*
 }
 
 template <int CB, int K, int NTG, bool FUSED>
-__global__ void __launch_bounds__(THREADS, CTAS_PER_SM) dense_kernel(const __grid_constant__ DenseParams p) {
+__global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_constant__ DenseParams p) {
     constexpr int TW = 8 * K;                          // words a tile
     constexpr int UNIT_W = 8 * TW;                     // words a unit (8 tiles)
     constexpr int MP = 8 * NTG;
@@ -594,8 +601,8 @@ size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks, int npre) {
            (fused ? (size_t)chunks * 8 * slice_w * 4 + (size_t)npre * 8 * 32 * 16 : 0) + 2 * STAGES * 8;
 }
 
-// dynamic shared memory a CTA may take: most of an SM's 227 KB with one CTA an SM, half of it with two
-constexpr size_t SMEM_LIMIT = (CTAS_PER_SM == 1 ? 220 : 110) * 1024;
+// dynamic shared memory a CTA may take: most of an SM's 227 KB with one resident CTA an SM, half of it with two
+constexpr size_t SMEM_LIMIT = (RESIDENT == 1 ? 220 : 110) * 1024;
 
 // ESPALIER_DENSE_AHEAD=0 turns the decode ahead of the launch wait off (for comparison); on by default.
 bool ahead_enabled() {
