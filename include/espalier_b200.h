@@ -258,6 +258,49 @@ int esp_ep_combine(const float* recv_y, const int* pick, const float* wts, void*
  */
 int esp_wait_flag(const int* flag, int need, int* result, void* stream);
 
+/*
+ * Expert-parallel exchange by stores into the other ranks' memory (the ranks of one NVLink box, one process a GPU).
+ * No counterpart in the reference (it has no expert parallelism); replaces the two all_to_all collectives of a layer.
+ *
+ * Set-up, once per rank (not on the decode path): esp_ipc_alloc allocates and zeroes `bytes` of device memory for this
+ * rank's inboxes and writes its CUDA IPC handle (esp_ipc_handle_bytes() bytes) to `handle`; the handles are exchanged
+ * by the host (any collective) and esp_ipc_open maps another rank's inboxes into this process (no multicast object);
+ * esp_ipc_close / esp_ipc_free undo them. Inboxes of a rank: x rows [world][R][D] (x's dtype), picks int32
+ * [world][R][slots], y fp32 [R][slots][D], flags_x and flags_y int32 [world]; plus a local epoch word and counters,
+ * zero at allocation. Every rank calls with the same R, slots and world; the calls of a layer are, in order:
+ *
+ *   esp_ep_dispatch  x [R][D] (row stride x_stride) and pick [R][slots] (global ids, the shared slot last) of this
+ *                    rank's rows: each row to the ranks that own one of its routed picks, every pick row to every
+ *                    rank; inbox_x / inbox_pick / flags_x: host arrays of every rank's inbox bases (this rank's own
+ *                    included)
+ *   esp_ep_recv      waits for every source's flag, writes local_pick int32 [world][R][slots] (local expert ids, the
+ *                    local shared entry for this rank's own shared slots, -1 elsewhere) for esp_group / esp_rot_in /
+ *                    the expert kernels
+ *   esp_ep_return    y fp32 [world][R][slots][D] (the expert kernels' per-slot output): each locally computed slot's
+ *                    row to its home rank's inbox (inbox_y / flags_y: host arrays of every rank's bases); done: int32
+ *                    [world] counters, zero, left zero
+ *   esp_ep_finish    waits for every owner's flag, then out / out_shared [R][D] as esp_ep_combine (slot-ordered fp32
+ *                    fused multiply-adds; bit-identical to one GPU); advances *epoch; count: an int32 counter
+ *
+ * Waits give up after 0.2 s and record ESP_ERR_TIMEOUT (esp_device_status). The epoch lives on the device, so a
+ * CUDA graph of the layer replays correctly.
+ */
+size_t esp_ipc_handle_bytes(void);
+int esp_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int esp_ipc_open(const void* handle, void** ptr);
+int esp_ipc_close(void* ptr);
+int esp_ipc_free(void* ptr);
+int esp_ep_dispatch(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots,
+                    int n_routed, int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick,
+                    int* const* flags_x, const int* epoch, void* stream);
+int esp_ep_recv(const int* inbox_pick, const int* flags_x, const int* epoch, int world, int rank, int R, int slots,
+                int n_routed, int E, int* local_pick, void* stream);
+int esp_ep_return(const float* y, const int* local_pick, int world, int rank, int R, int slots, int D,
+                  float* const* inbox_y, int* const* flags_y, const int* epoch, int* done, void* stream);
+int esp_ep_finish(const float* inbox_y, const int* flags_y, const int* pick, const float* wts, void* out,
+                  void* out_shared, int out_dtype, int R, int D, int slots, int n_routed, int E, int world, int* epoch,
+                  int* count, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

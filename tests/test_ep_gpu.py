@@ -1,6 +1,7 @@
-"""Expert-parallel MoE layer on 2, 4 and 8 GPUs (NCCL): each rank's EPLayer output must equal, bit for bit, the
-single-GPU fused path (route + routed2) on a layer holding every expert, for the same rows. Each world size is skipped
-on a box with fewer GPUs.
+"""Expert-parallel MoE layer on 2, 4 and 8 GPUs, with either exchange (p2p: peer stores and flags, the default; nccl:
+two all_to_all collectives): each rank's EPLayer output must equal, bit for bit, the single-GPU fused path (route +
+routed2) on a layer holding every expert, for the same rows, on two calls in a row (the second runs on the advanced
+epoch and the inboxes the first left). Each world size is skipped on a box with fewer GPUs.
 
 One case biases the router so that one expert is picked by every row: the 32 rows of every rank then give that expert
 32 x world members, more than a grouping entry holds (32), which exercises the chunked grouping."""
@@ -38,10 +39,10 @@ def _bf(a_bits, dev):
     return torch.from_numpy(np.ascontiguousarray(a_bits).view(np.int16)).to(dev).view(torch.bfloat16)
 
 
-def _worker(rank, world, port, R, bias, q):
+def _worker(rank, world, port, R, bias, exchange, q):
     import datetime
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), ESPALIER_EP_EXCHANGE=exchange)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -71,25 +72,34 @@ def _worker(rank, world, port, R, bias, q):
         e0, e1 = ep.expert_range(rank, world, E)
         mine = mats()
         epl = ep.EPLayer(mine[e0:e1], mine[-1], _bf(gate_w, dev), rank, world, E, rows=32, k=k)
-        got, got_sh = epl.forward(x, gate_b)
-        torch.cuda.synchronize()
+        assert epl.exchange == exchange
+        same = True
+        for _ in range(2):
+            got, got_sh = epl.forward(x, gate_b)
+            torch.cuda.synchronize()
+            same &= bool(torch.equal(got, want)) and bool(torch.equal(got_sh, want_sh))
         n_entries = int(epl.count.item())
-        q.put((rank, bool(torch.equal(got, want)), bool(torch.equal(got_sh, want_sh)),
-               float((got.float() - want.float()).abs().max()), n_entries))
+        from vllm_espalier_b200 import _lib
+        status = _lib.device_status()
+        dist.barrier()
+        if epl.ex is not None:
+            epl.ex.close()
+        q.put((rank, same, status == 0, float((got.float() - want.float()).abs().max()), n_entries))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("R,bias", [(3, False), (32, False), (32, True)])
-def test_ep_bitwise_equal_to_one_gpu(world, R, bias):
+def test_ep_bitwise_equal_to_one_gpu(world, R, bias, exchange):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(rk, world, port, R, bias, q)) for rk in range(world)]
+    procs = [ctx.Process(target=_worker, args=(rk, world, port, R, bias, exchange, q)) for rk in range(world)]
     for p in procs:
         p.start()
     for p in procs:

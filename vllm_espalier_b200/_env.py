@@ -17,3 +17,4 @@ FUSED_ROUTING = flag("ESPALIER_FUSED_ROUTING")        # fused router GEMV + top-
 MOE_ONE_LAUNCH = flag("ESPALIER_MOE_FUSED")          # gate/up and down of the experts in one launch (this library)
 PREFILL = env("ESPALIER_PREFILL_MODE", "chunk")       # chunk | gemm
 DEBUG_SHARED_FOLD = flag("ESPALIER_DEBUG_SHARED_FOLD", "0")
+EP_EXCHANGE = env("ESPALIER_EP_EXCHANGE", "p2p")   # expert parallelism: p2p (peer stores) | nccl (all_to_all)

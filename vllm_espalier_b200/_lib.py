@@ -61,6 +61,15 @@ SIGNATURES = {
                           P, P, P, P, P, P, I, P]),
     "esp_moe_layer_counters": (S, [I, I, I, I]),
     "esp_dense_z_bytes": (S, [I]),
+    "esp_ipc_handle_bytes": (S, []),
+    "esp_ipc_alloc": (I, [S, C.POINTER(P), P]),
+    "esp_ipc_open": (I, [P, C.POINTER(P)]),
+    "esp_ipc_close": (I, [P]),
+    "esp_ipc_free": (I, [P]),
+    "esp_ep_dispatch": (I, [P, I, L, I, I, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), C.POINTER(P), P, P]),
+    "esp_ep_recv": (I, [P, P, P, I, I, I, I, I, I, P, P]),
+    "esp_ep_return": (I, [P, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), P, P, P]),
+    "esp_ep_finish": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P]),
 }
 
 

@@ -14,6 +14,7 @@ namespace esp {
 int status_dense(int reset);   // one reader per translation unit that has device waits
 int status_route(int reset);
 int status_moe(int reset);
+int status_ep(int reset);
 
 namespace {
 thread_local char t_msg[512] = "";
@@ -65,7 +66,7 @@ int esp_sm_count(void) { return esp::device_sms(); }
 int esp_device_status(int* status, int reset) {
     if (!status) return esp::set_error(ESP_ERR_INVALID, "esp_device_status: status is NULL");
     int v = 0;
-    for (int (*rd)(int) : {esp::status_dense, esp::status_route, esp::status_moe}) {
+    for (int (*rd)(int) : {esp::status_dense, esp::status_route, esp::status_moe, esp::status_ep}) {
         const int s = rd(reset);
         if (s < 0) return esp::set_error(ESP_ERR_CUDA, "esp_device_status: %s", cudaGetErrorString(cudaGetLastError()));
         if (!v) v = s;

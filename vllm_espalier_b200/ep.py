@@ -16,13 +16,20 @@ layer, with outputs bit-identical to it for every world size:
     row's routed slots in slot order with fp32 fused multiply-adds from 0 (esp_ep_combine): the single-GPU kernel's
     arithmetic on the same y values, hence the same output bits.
 
-The index logic (local tables, owners, buffer layouts) is in plain torch functions shared by the GPU path and the
-CPU tests (gloo ranks with a stand-in expert function).
+The exchange (ESPALIER_EP_EXCHANGE): `p2p` (default) moves rows and results by stores into the other ranks' memory
+(csrc/ep.cu, PeerExchange below): a row goes only to the ranks owning one of its picks, a slot's y row only from its
+owner to its home rank, with release / acquire flags instead of collectives, 4 small launches around the expert
+kernels and nothing on the host; `nccl` is the two-collective form above. The index logic of the `nccl` form (local
+tables, owners, buffer layouts) is in plain torch functions shared with the CPU tests (gloo ranks with a stand-in
+expert function); the `p2p` form computes the same table on the device (esp_ep_recv).
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
+from ._env import EP_EXCHANGE
 from ._lib import DTYPE, check, ext, lib, stream_ptr
 from . import experts as X
 
@@ -78,6 +85,64 @@ def give_back(y: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+def _device_view(ptr: int, n: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """A torch tensor over n elements of raw device memory (no copy), through the CUDA array interface."""
+    typestr = {torch.int32: "<i4", torch.float32: "<f4", torch.int16: "<i2"}[torch.int16 if dtype.itemsize == 2 else dtype]
+
+    class _Raw:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+    t = torch.as_tensor(_Raw(), device=device)
+    return t.view(dtype) if dtype.itemsize == 2 else t
+
+
+class PeerExchange:
+    """This rank's inboxes (one allocation, shared with every other rank through a CUDA IPC handle) and the mapped
+    inboxes of the others, for rows of up to `rows` tokens a rank: x [world][rows][D], picks [world][rows][slots],
+    y fp32 [rows][slots][D], flags_x / flags_y [world], the epoch, counters. Built once per layer at set-up."""
+
+    LAYOUT = ("x", "pick", "y", "flags_x", "flags_y", "epoch", "done", "count")
+
+    def __init__(self, rank: int, world: int, rows: int, D: int, slots: int, dtype: torch.dtype, device, group=None):
+        import torch.distributed as dist
+        h = lib()
+        sizes = {"x": world * rows * D * dtype.itemsize, "pick": world * rows * slots * 4, "y": rows * slots * D * 4,
+                 "flags_x": world * 4, "flags_y": world * 4, "epoch": 4, "done": world * 4, "count": 4}
+        self.offset, total = {}, 0
+        for name in self.LAYOUT:
+            self.offset[name] = total
+            total += -(-sizes[name] // 256) * 256
+        base, handle = C.c_void_p(), (C.c_char * int(h.esp_ipc_handle_bytes()))()
+        check(h.esp_ipc_alloc(total, C.byref(base), handle))
+        self.base, self.rank, self.world = base.value, rank, world
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases, self.opened = [], []
+        for q in range(world):
+            if q == rank:
+                self.bases.append(self.base)
+                continue
+            p = C.c_void_p()
+            check(h.esp_ipc_open(C.create_string_buffer(handles[q], len(handles[q])), C.byref(p)))
+            self.bases.append(p.value)
+            self.opened.append(p.value)
+        self.peer = {name: (C.c_void_p * world)(*[b + self.offset[name] for b in self.bases])
+                     for name in ("x", "pick", "y", "flags_x", "flags_y")}
+        self.inbox_x = _device_view(self.local("x"), world * rows * D, dtype, device).view(world * rows, D)
+        self.lp = torch.full((world * rows * slots,), -1, dtype=torch.int32, device=device)
+
+    def local(self, name: str) -> int:
+        return self.base + self.offset[name]
+
+    def close(self):
+        h = lib()
+        for p in self.opened:
+            h.esp_ipc_close(C.c_void_p(p))
+        self.opened = []
+        if self.base:
+            h.esp_ipc_free(C.c_void_p(self.base))
+            self.base = 0
+
+
 class EPLayer:
     """One MoE layer's local share on this rank. `local_experts`: the (gate, up, down) matrices of experts
     [e0, e1) = expert_range(rank, world, E); `shared`: the shared expert's, `gate_w` its sigmoid-gate weight."""
@@ -114,6 +179,8 @@ class EPLayer:
         self.cnt_d = torch.zeros((world * rows * (D // 128) + 1,), dtype=torch.int32, device=dev)
         self.no_w = torch.zeros((P,), dtype=torch.float32, device=dev)
         self.no_out = torch.empty((world * rows, D), dtype=torch.bfloat16, device=dev)
+        self.exchange = EP_EXCHANGE
+        self.ex = None          # the PeerExchange, made at the first p2p forward (it needs the rows' dtype)
 
     def route(self, x: torch.Tensor, gate: torch.Tensor):
         """Fused routing of this rank's rows -> (pick int32 [R][slots], wts fp32 [R][slots]), global ids."""
@@ -125,29 +192,33 @@ class EPLayer:
         return s.pick[:R * self.slots].view(R, self.slots), s.wts[:R * self.slots].view(R, self.slots)
 
     def experts(self, recv_x: torch.Tensor, lp: torch.Tensor) -> torch.Tensor:
-        """y fp32 [world][R][slots][D] of the local experts for every received (row, slot) with a local pick."""
-        e = ext()
+        """y fp32 [world][R][slots][D] of the local experts for every received (row, slot) with a local pick; recv_x
+        [world][R][D] (any row stride)."""
         world, R, D = recv_x.shape
-        rows, slots = world * R, self.slots
-        P = rows * slots
         if R > self.rows:
             raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
+        self._run_experts(recv_x, recv_x.stride(1), world * R, lp.reshape(-1))
+        return self.y[:world * R * self.slots].view(world, R, self.slots, D)
+
+    def _run_experts(self, rows_x, stride: int, rows: int, lpf: torch.Tensor):
+        e = ext()
+        D, slots = self.L.D, self.slots
+        P = rows * slots
         L = self.L
-        lpf = lp.reshape(-1)
-        stride = recv_x.stride(1)                 # rows of the packed dispatch buffer: D values, then the picks
         e.group(lpf, self.ids, self.count, self.members, rows, slots, self.nl + 1)
-        e.rot_in(recv_x, stride, lpf, L.gate.suh, L.up.suh, self.xg, self.xu, rows, D, slots, self.nl + 1)
+        e.rot_in(rows_x, stride, lpf, L.gate.suh, L.up.suh, self.xg, self.xu, rows, D, slots, self.nl + 1)
         e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, P, self.S, self.z, self.cnt_gu,
                      self.xd)
         e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
                    self.cnt_d, self.no_out[:rows], None)
-        return self.y[:P].view(world, R, slots, D)
 
     def forward(self, x: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
                 out_shared: torch.Tensor | None = None, group=None):
         """x [R, D] bf16/fp16 (this rank's rows), gate [E, D] the router -> (routed sum, shared output), [R, D] in x's
         dtype, bit-identical to experts.routed2 on one GPU holding every expert."""
         R, D = x.shape
+        if self.exchange == "p2p":
+            return self._forward_p2p(x, gate, out, out_shared, group)
         pick, wts = self.route(x, gate)
         recv_x, recv_p = dispatch(x, pick, self.world, group)
         lp = local_table(recv_p, self.rank, self.world, self.E, self.k)
@@ -158,4 +229,30 @@ class EPLayer:
         check(lib().esp_ep_combine(back.data_ptr(), pick.data_ptr(), wts.data_ptr(), out.data_ptr(),
                                    out_shared.data_ptr(), DTYPE[out.dtype], R, D, self.slots, self.k, self.E,
                                    self.world, self.rank, stream_ptr(x.device)))
+        return out, out_shared
+
+    def _forward_p2p(self, x, gate, out, out_shared, group):
+        """The same layer with the peer-store exchange: route, dispatch, receive, experts, return, finish."""
+        R, D = x.shape
+        if R > self.rows:
+            raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
+        if self.ex is None:
+            self.ex = PeerExchange(self.rank, self.world, self.rows, D, self.slots, x.dtype, x.device, group)
+        ex, h, st = self.ex, lib(), stream_ptr(x.device)
+        world, rank, slots, k = self.world, self.rank, self.slots, self.k
+        pick, wts = self.route(x, gate)
+        x = x if x.stride(1) == 1 else x.contiguous()
+        check(h.esp_ep_dispatch(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, D, pick.data_ptr(), slots, k, self.E,
+                                world, rank, ex.peer["x"], ex.peer["pick"], ex.peer["flags_x"], ex.local("epoch"), st))
+        lp = ex.lp[:world * R * slots]
+        check(h.esp_ep_recv(ex.local("pick"), ex.local("flags_x"), ex.local("epoch"), world, rank, R, slots, k, self.E,
+                            lp.data_ptr(), st))
+        self._run_experts(ex.inbox_x, D, world * R, lp)
+        check(h.esp_ep_return(self.y.data_ptr(), lp.data_ptr(), world, rank, R, slots, D, ex.peer["y"],
+                              ex.peer["flags_y"], ex.local("epoch"), ex.local("done"), st))
+        out = out if out is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
+        out_shared = out_shared if out_shared is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
+        check(h.esp_ep_finish(ex.local("y"), ex.local("flags_y"), pick.data_ptr(), wts.data_ptr(), out.data_ptr(),
+                              out_shared.data_ptr(), DTYPE[out.dtype], R, D, slots, k, self.E, world, ex.local("epoch"),
+                              ex.local("count"), st))
         return out, out_shared
