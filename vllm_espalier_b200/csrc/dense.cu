@@ -49,6 +49,12 @@ constexpr int CWARPS = 8 * GROUPS;             // consumer warps: warp w decodes
 #endif
 constexpr int PRODUCERS = ESP_DENSE_PRODUCERS;  // producer warps: unit j of a stage goes to producer j % PRODUCERS
 constexpr int THREADS = (CWARPS + PRODUCERS) * 32;
+#ifndef ESP_DENSE_BULK
+#define ESP_DENSE_BULK 0
+#endif
+// 1: the fused path's producers move each unit with one 1-D bulk copy (cp.async.bulk, mbarrier transaction count)
+// from one lane instead of 16-byte cp.async from all lanes (a measured alternative; off by default)
+constexpr bool BULK = ESP_DENSE_BULK != 0;
 constexpr int UPS = 8;                         // units per pipeline stage
 constexpr int STAGES = 6;                      // pipeline depth (stages of UPS units)
 constexpr int RED_STRIDE = 132;                // fp32 row stride of the reduction buffer (bank-conflict free)
@@ -208,6 +214,7 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
     constexpr int MP = 8 * NTG;
     constexpr int SLICE_W = MP * 8;                    // words of a k-tile's activation slice
     constexpr int STAGE_W = UPS * (UNIT_W + (FUSED ? 0 : SLICE_W));
+    constexpr bool BULKW = FUSED && BULK;
     extern __shared__ __align__(128) uint32_t smem[];
     float* red = reinterpret_cast<float*>(smem + (size_t)STAGES * STAGE_W);   // [MP][RED_STRIDE]
     uint32_t* xrot = reinterpret_cast<uint32_t*>(red + MP * RED_STRIDE);      // fused: [chunks][8][2][MP][4]
@@ -225,7 +232,8 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&full[i], 32 * PRODUCERS);   // one arrival a producer lane, when its copies have landed
+            // one arrival a producer lane when its copies have landed; bulk copies: one a producer, with its bytes
+            mbar_init(&full[i], BULKW ? PRODUCERS : 32 * PRODUCERS);
             mbar_init(&empty[i], CWARPS);
         }
         fence_mbar_init();
@@ -268,6 +276,13 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
         auto fill = [&](int i, int slot, bool w, bool x, Cur& q) {
             const uint32_t st = sbase + (uint32_t)slot * (STAGE_W * 4);
             const int m = min(UPS, n - i * UPS);
+            if constexpr (BULKW) {   // weights only (fused path): lane 0 announces this producer's bytes and copies
+                const int mine = m > pw ? (m - pw + PRODUCERS - 1) / PRODUCERS : 0;
+                if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(mine * UNIT_W * 4));
+                for (int j = pw; j < m; j += PRODUCERS, step2(q))
+                    if (lane == 0) bulk_g2s(st + j * UNIT_W * 4, src_w(q), UNIT_W * 4, &full[slot]);
+                return;
+            }
             for (int j = pw; j < m; j += PRODUCERS, step2(q)) {
                 if (w) {
                     const uint32_t* src = src_w(q);
@@ -286,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
         if constexpr (FUSED) {
             for (int i = 0; i < pre; ++i) {
                 fill(i, i, true, false, cur);
-                cp_async_arrive(&full[i]);
+                if (!BULKW) cp_async_arrive(&full[i]);
             }
         } else {
             // weights do not depend on the previous kernel: fetch them first, then (after the wait) the activations
@@ -301,7 +316,7 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
         for (int i = STAGES, slot = 0, phase = 0; i < nst; ++i) {
             if (!mbar_wait(&empty[slot], phase)) break;   // gave up (status recorded)
             fill(i, slot, true, !FUSED, cur);
-            cp_async_arrive(&full[slot]);
+            if (!BULKW) cp_async_arrive(&full[slot]);
             if (++slot == STAGES) {
                 slot = 0;
                 phase ^= 1;
