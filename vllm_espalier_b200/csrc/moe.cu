@@ -716,6 +716,39 @@ struct FinEntry {
     int e, nm;                     // the entry's expert and member count
     float c0, c1;                  // codebook steps (gate, up)
 };
+// Warm the L2 with data of this layer that is not the previous kernel's output, while that kernel still runs (before
+// the launch wait): the expert tables (CTA 0, 128-byte lines) and the three matrices of the last table entry, which is
+// the shared expert whenever the layer has one (every call uses it; otherwise a routed expert, harmlessly), a slice a
+// CTA by one bulk L2 prefetch each. Every layer has tables and experts of its own, so both would be DRAM misses.
+__device__ __forceinline__ void prefetch_line_l2(const void* a) { asm volatile("prefetch.global.L2 [%0];" ::"l"(a)); }
+__device__ __forceinline__ void bulk_prefetch_l2(const void* a, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(bytes) : "memory");
+}
+
+template <typename LP>
+__device__ __forceinline__ void layer_prefetch(const LP& p, int threads) {
+    if (blockIdx.x == 0) {
+        const int l8 = (p.E * 8 + 127) / 128, l4 = (p.E * 4 + 127) / 128, per = l8 + 2 * l4;
+        for (int i = threadIdx.x; i < 3 * per; i += threads) {
+            const int t = i / per, j = i % per;
+            const char* a = j < l8 ? reinterpret_cast<const char*>(p.tp[t]) + 128 * j
+                          : j < l8 + l4 ? reinterpret_cast<const char*>(p.k2[t]) + 128 * (j - l8)
+                                        : reinterpret_cast<const char*>(p.cb[t]) + 128 * (j - l8 - l4);
+            prefetch_line_l2(a);
+        }
+    }
+    if (threadIdx.x == 0) {
+        const int e = p.E - 1;
+        for (int t = 0; t < 3; ++t) {
+            const size_t bytes = (size_t)p.D * p.I * (p.k2[t][e] / 2) / 8;   // a multiple of 16 (D, I multiples of 128)
+            const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+            const size_t off = (size_t)blockIdx.x * per;
+            if (off < bytes)
+                bulk_prefetch_l2(reinterpret_cast<const char*>(p.tp[t][e]) + off, (uint32_t)min(per, bytes - off));
+        }
+    }
+}
+
 constexpr int FQ = 32;                             // finisher queue entries
 constexpr int LMAXP = 32 * 32;                     // slots a call (32 rows x 32 slots at most)
 constexpr int LWARPS = GWARPS + GPROD + 1;         // + the finisher warp
@@ -786,6 +819,7 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
     const int NBg = p.I / 128, NBd = p.D / 128;
     const int KTg = p.D / 16, KTd = p.I / 16;
     const int P = p.rows * p.slots;
+    layer_prefetch(p, LTHREADS);
     pdl_launch_dependents();
     pdl_wait();
     const int nu = p.ucount[0];
