@@ -127,6 +127,18 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
                     int* uids, int* ucount, int* members, int maxm, int maxu, void* stream);
 
 /*
+ * esp_route_group plus the experts' input rotation in the same launch (this library's fused form, no single counterpart
+ * in the reference, which launches rot_in after its routing, experts.py:245-247): once the picks are written, every CTA
+ * of the launch computes a share of out0 / out1 [R * slots][H] = fp16(H(x[row] * suh0 / suh1[e]) / sqrt(128)) per
+ * 128-block for each slot with a pick e in [0, E_tab), exactly as esp_rot_in. suh0 / suh1: stacked fp16 [E_tab][H].
+ * counter: 3 int32 words, zero on entry and left zero.
+ */
+int esp_route_rot(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                  const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                  int* uids, int* ucount, int* members, int maxm, int maxu, const uint16_t* suh0,
+                  const uint16_t* suh1, uint16_t* out0, uint16_t* out1, int E_tab, void* stream);
+
+/*
  * Grouping of a given pick table pick[R][slots] (ids outside [0, E) are skipped).
  * Replaces ext().group(pick, uids, ucount, members, R, slots, E)  (vllm_espalier/csrc/experts.cpp:79-90,
  *                                                                    experts.cu:23-76).

@@ -327,3 +327,33 @@ def test_one_launch_layer_equals_two_launches(dev, monkeypatch, R):
         assert torch.equal(o, a) and torch.equal(sh, b)
     assert _lib.device_status() == 0
     assert int(s.cnt_layer.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("R", [1, 8, 32])
+def test_route_with_rotation_equals_route_then_rot_in(dev, R):
+    """The routing launch's folded input rotation (esp_route_rot) writes exactly rot_in's xg / xu, and the same picks,
+    weights and grouping as esp_route_group; its counters come back to zero."""
+    ex_np, gate_b, sgate_b = _config3_layer(dev)
+    mats = build(ex_np, dev)
+    L = G.prepare(mats[:-1], mats[-1], bf(sgate_b, dev))
+    k = 8
+    s = G.scratch(L, 32, k + 1, dev)
+    x = bf(C.activations(("route-rot", R), R, 2048), dev)
+    gate = bf(gate_b, dev)
+    P = R * (k + 1)
+    G.route(x, gate, k, L, s)                     # routing with the folded rotation
+    torch.cuda.synchronize()
+    got = [t[:P].clone() for t in (s.xg, s.xu, s.pick, s.wts)] + [s.count.clone()]
+    s.rotated = False
+    s.xg.zero_()
+    s.xu.zero_()
+    ids, members = s.window(R)
+    _lib.ext().route_group(x, gate, L.gate_w, k, L.shared_id, s.logits, s.route_counter, s.pick[:P], s.wts[:P], ids,
+                           s.count, members)
+    _lib.ext().rot_in(x, x.stride(0), s.pick[:P], L.gate.suh, L.up.suh, s.xg, s.xu, R, 2048, k + 1, L.E)
+    torch.cuda.synchronize()
+    want = [t[:P] for t in (s.xg, s.xu, s.pick, s.wts)] + [s.count]
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    assert int(s.route_counter.abs().sum()) == 0
+    assert _lib.device_status() == 0

@@ -61,6 +61,7 @@ SIGNATURES = {
                           P, P, P, P, P, P, I, P]),
     "esp_moe_layer_counters": (S, [I, I, I, I]),
     "esp_dense_z_bytes": (S, [I]),
+    "esp_route_rot": (I, [P, I, L, I, I, P, I, P, I, I, P, P, P, P, P, P, P, I, I, P, P, P, P, I, P]),
     "esp_ipc_handle_bytes": (S, []),
     "esp_ipc_alloc": (I, [S, C.POINTER(P), P]),
     "esp_ipc_open": (I, [P, C.POINTER(P)]),
@@ -182,7 +183,10 @@ class _Ext:
 
     # ---- MoE (experts.cpp:44-190, 214-223) ----
     @staticmethod
-    def route_group(x, gate, sgate, k, shared_id, logits, counter, pick_out, wts_out, uids, ucount, members):
+    def route_group(x, gate, sgate, k, shared_id, logits, counter, pick_out, wts_out, uids, ucount, members,
+                    rotate=None):
+        """rotate = (suh_g, suh_u, xg, xu, E_tables): this library's fused form, which also writes rot_in's output
+        (counter: 3 int32 words)."""
         _need(x.is_cuda and x.dim() == 2 and x.stride(1) == 1 and gate.is_contiguous(), "x / gate layout")
         _need(gate.dtype == x.dtype and x.dtype in (torch.bfloat16, torch.float16), "gate and x must share a dtype")
         _check(logits, torch.float32, "logits")
@@ -192,10 +196,18 @@ class _Ext:
         has = shared_id >= 0
         _need(logits.numel() >= R * (E + has), "logits scratch too small")
         maxm = members.size(1) if members.dim() == 2 else R
-        check(lib().esp_route_group(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, H, gate.data_ptr(), E,
-                                    ptr(sgate), int(k), int(shared_id), logits.data_ptr(), counter.data_ptr(),
-                                    pick_out.data_ptr(), wts_out.data_ptr(), uids.data_ptr(), ucount.data_ptr(),
-                                    members.data_ptr(), maxm, uids.numel(), stream_ptr(x.device)))
+        args = (x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, H, gate.data_ptr(), E, ptr(sgate), int(k),
+                int(shared_id), logits.data_ptr(), counter.data_ptr(), pick_out.data_ptr(), wts_out.data_ptr(),
+                uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), maxm, uids.numel())
+        if rotate is None:
+            check(lib().esp_route_group(*args, stream_ptr(x.device)))
+            return
+        suh0, suh1, out0, out1, e_tab = rotate
+        _need(counter.numel() >= 3, "counter: 3 int32 words for the fused rotation")
+        for t, n in ((suh0, "suh_g"), (suh1, "suh_u"), (out0, "xg"), (out1, "xu")):
+            _check(t, torch.float16, n)
+        check(lib().esp_route_rot(*args, suh0.data_ptr(), suh1.data_ptr(), out0.data_ptr(), out1.data_ptr(),
+                                  int(e_tab), stream_ptr(x.device)))
 
     @staticmethod
     def group(pick, uids, ucount, members, R, slots, E):

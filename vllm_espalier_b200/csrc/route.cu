@@ -258,6 +258,62 @@ __device__ void group_distinct(const int* sh_pick, int R, int slots, int n_ids, 
     }
 }
 
+// The experts' input rotation folded into the routing launch (esp_route_rot): once the last CTA has written the picks,
+// every CTA of the launch (one wave, all resident) rotates a share of the (matrix, slot, 128-block) items:
+// out_m[p] = fp16(H(x[row] * suh_m[e]) / sqrt(128)), rot_in's arithmetic, for each slot p with a pick e in [0, E_tab).
+struct RotIn {
+    const __half* suh[2];          // stacked [E_tab][H] (gate, up); null: no rotation
+    __half* out[2];                // [R * slots][H]
+    int E_tab;
+};
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// one thread: wait until *flag >= need (GPU-scope acquire), bounded by time
+__device__ bool wait_flag_gpu(const int* flag, int need) {
+    if (ld_acquire_gpu(flag) >= need) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        for (int i = 0; i < 32; ++i) {
+            __nanosleep(32);
+            if (ld_acquire_gpu(flag) >= need) return true;
+        }
+        const uint64_t dt = global_ns() - t0;
+        if (dt > WAIT_NS) break;
+        if (dt > 20000 && *reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT) return false;
+    }
+    report(ESP_ERR_TIMEOUT);
+    return false;
+}
+
+template <typename T>
+__device__ void rotate_share(const T* __restrict__ x, long long x_stride, int H, const int* pick, int P, int slots,
+                             const RotIn& rot) {
+    const int lane = threadIdx.x & 31;
+    const int nblk = H / 128, ntask = 2 * P * nblk;
+    const int nw = gridDim.x * gridDim.y * RW;
+    for (int w = (blockIdx.y * gridDim.x + blockIdx.x) * RW + (threadIdx.x >> 5); w < ntask; w += nw) {
+        const int mat = w / (P * nblk), rem = w % (P * nblk), p = rem / nblk, blk = rem % nblk;
+        const int e = __ldcg(pick + p);
+        if (e < 0 || e >= rot.E_tab) continue;
+        const int k0 = blk * 128 + 4 * lane;
+        const __half* su = rot.suh[mat] + (size_t)e * H + k0;
+        const T* xr = x + (size_t)(p / slots) * x_stride + k0;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(to_f<T>(xr[j]), __half2float(su[j]));
+        fwht128(v, lane);
+        const __half2 a = __floats2half2_rn(v[0] * HAD_SCALE, v[1] * HAD_SCALE);
+        const __half2 b = __floats2half2_rn(v[2] * HAD_SCALE, v[3] * HAD_SCALE);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&a);
+        u.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(rot.out[mat] + (size_t)p * H + k0) = u;
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long long x_stride, int R, int H,
                                                    const T* __restrict__ gate, int E, const T* __restrict__ sgate,
@@ -265,7 +321,7 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
                                                    int* __restrict__ counter, int* __restrict__ pick_out,
                                                    float* __restrict__ wts_out, int* __restrict__ uids,
                                                    int* __restrict__ ucount, int* __restrict__ members, int maxm,
-                                                   int maxu, int rpc) {
+                                                   int maxu, int rpc, const RotIn rot) {
     __shared__ int last;
     __shared__ int sh_pick[MAX_PICKS];
     extern __shared__ float sh_logit[];    // [R][C], the last CTA's copy of the logits
@@ -294,7 +350,22 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
         last = arrive_acq_rel(counter) == (int)(gridDim.x * gridDim.y) - 1;
     }
     __syncthreads();
-    if (!last) return;
+    const int ncta = gridDim.x * gridDim.y;
+    if (!last) {
+        if (!rot.suh[0]) return;
+        // the rotation share of this CTA once the last CTA has published the picks (counter[1]); counter[2] counts
+        // the CTAs done, the last of which clears both words for the next call
+        __shared__ int ok;
+        if (threadIdx.x == 0) ok = wait_flag_gpu(counter + 1, 1);
+        __syncthreads();
+        if (ok) rotate_share<T>(x, x_stride, H, pick_out, R * (k + (shared_id >= 0)), k + (shared_id >= 0), rot);
+        __syncthreads();
+        if (threadIdx.x == 0 && arrive_acq_rel(counter + 2) == ncta - 1) {
+            counter[1] = 0;
+            counter[2] = 0;
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < R * C; i += RT) sh_logit[i] = __ldcg(logits + i);   // one round of loads
     __syncthreads();
 
@@ -339,8 +410,22 @@ __global__ void __launch_bounds__(RT) route_kernel(const T* __restrict__ x, long
         }
     }
     __syncthreads();   // the picks are in sh_pick (written beside pick_out above)
+    if (rot.suh[0]) {   // publish the picks to the other CTAs first: their rotation overlaps the grouping
+        if (threadIdx.x == 0) {
+            __threadfence();
+            st_release_gpu(counter + 1, 1);
+        }
+    }
     group_distinct(sh_pick, R, slots, E + has, uids, ucount, members, maxm, maxu);
     if (threadIdx.x == 0) *counter = 0;
+    if (rot.suh[0]) {
+        rotate_share<T>(x, x_stride, H, pick_out, R * slots, slots, rot);
+        __syncthreads();
+        if (threadIdx.x == 0 && arrive_acq_rel(counter + 2) == ncta - 1) {
+            counter[1] = 0;
+            counter[2] = 0;
+        }
+    }
 }
 
 // group (experts.cu:23-76): the grouping of a given pick table.
@@ -401,16 +486,9 @@ __global__ void __launch_bounds__(RT) group_shared_kernel(const int* __restrict_
     group_block(sh_pick, n, slots, E, uids, ucount, members, maxm, maxu);
 }
 
-}  // namespace
-}  // namespace esp
-
-using namespace esp;
-
-extern "C" {
-
-int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
-                    const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
-                    int* uids, int* ucount, int* members, int maxm, int maxu, void* stream) {
+int route_launch(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                 const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                 int* uids, int* ucount, int* members, int maxm, int maxu, const RotIn& rot, void* stream) {
     ESP_REQUIRE(x && gate && logits && counter && pick_out && wts_out && uids && ucount && members, ESP_ERR_INVALID,
                 "route_group: null pointer");
     const int has = shared_id >= 0;
@@ -442,13 +520,44 @@ int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H
         rc = launch(route_kernel<__nv_bfloat16>, grid, dim3(RT), smem, stream, true,
                     static_cast<const __nv_bfloat16*>(x), x_stride, R, H, static_cast<const __nv_bfloat16*>(gate), E,
                     static_cast<const __nv_bfloat16*>(sgate), k, shared_id, logits, counter, pick_out, wts_out, uids,
-                    ucount, members, maxm, maxu, ppc * RB);
+                    ucount, members, maxm, maxu, ppc * RB, rot);
     else
         rc = launch(route_kernel<__half>, grid, dim3(RT), smem, stream, true, static_cast<const __half*>(x), x_stride,
                     R, H, static_cast<const __half*>(gate), E, static_cast<const __half*>(sgate), k, shared_id, logits,
-                    counter, pick_out, wts_out, uids, ucount, members, maxm, maxu, ppc * RB);
+                    counter, pick_out, wts_out, uids, ucount, members, maxm, maxu, ppc * RB, rot);
     if (rc) return rc;
     return ok();
+}
+
+}  // namespace
+}  // namespace esp
+
+using namespace esp;
+
+extern "C" {
+
+int esp_route_group(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                    const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                    int* uids, int* ucount, int* members, int maxm, int maxu, void* stream) {
+    return route_launch(x, x_dtype, x_stride, R, H, gate, E, sgate, k, shared_id, logits, counter, pick_out, wts_out,
+                        uids, ucount, members, maxm, maxu, RotIn{}, stream);
+}
+
+int esp_route_rot(const void* x, int x_dtype, long long x_stride, int R, int H, const void* gate, int E,
+                  const void* sgate, int k, int shared_id, float* logits, int* counter, int* pick_out, float* wts_out,
+                  int* uids, int* ucount, int* members, int maxm, int maxu, const uint16_t* suh0,
+                  const uint16_t* suh1, uint16_t* out0, uint16_t* out1, int E_tab, void* stream) {
+    ESP_REQUIRE(suh0 && suh1 && out0 && out1 && E_tab >= 1, ESP_ERR_INVALID, "route_rot: rotation buffers");
+    ESP_REQUIRE(H % 128 == 0 && aligned(suh0, 8) && aligned(suh1, 8) && aligned(out0, 8) && aligned(out1, 8),
+                ESP_ERR_INVALID, "route_rot: 8-byte aligned rotation buffers");
+    RotIn rot = {};
+    rot.suh[0] = reinterpret_cast<const __half*>(suh0);
+    rot.suh[1] = reinterpret_cast<const __half*>(suh1);
+    rot.out[0] = reinterpret_cast<__half*>(out0);
+    rot.out[1] = reinterpret_cast<__half*>(out1);
+    rot.E_tab = E_tab;
+    return route_launch(x, x_dtype, x_stride, R, H, gate, E, sgate, k, shared_id, logits, counter, pick_out, wts_out,
+                        uids, ucount, members, maxm, maxu, rot, stream);
 }
 
 int esp_group(const int* pick, int R, int slots, int E, int* uids, int* ucount, int* members, int maxm, int maxu,

@@ -4,9 +4,9 @@ Surface kept from the reference (vllm_espalier/experts.py): prepare(experts, sha
 scratch(layer, rows, slots, device) -> Scratch, route, routed2, windows, routed, dequant. The layer runs as
 
   route      (fused routing launch) router logits, softmax, top-k, renormalised weights, the shared expert as one more
-             slot with its sigmoid gate, and the grouping: distinct experts in id order, members in (row, slot) order;
-             or, given vLLM's picks, group_shared does the last two
-  rot_in     H(x * suh) of every slot for gate and up
+             slot with its sigmoid gate, the grouping (distinct experts in id order, members in (row, slot) order) and,
+             once the picks are out, H(x * suh) of every slot for gate and up, shared by all the launch's CTAs;
+  rot_in     given vLLM's picks instead: group_shared does the shared slot and the grouping, rot_in the rotation
   moe_layer  one persistent launch: gate and up of every distinct expert (weights decoded in registers, K in S
              slices), the SwiGLU epilogue, down, and each row's slot-ordered weighted sum written in x's dtype
              (ESPALIER_MOE_FUSED=0: the same work as two launches, moe_gateup then moe_down, same bits)
@@ -130,7 +130,7 @@ class Scratch:
         spec = {   # name: (elements, dtype, initial value)
             "xg": (P * D, torch.float16, 0), "xu": (P * D, torch.float16, 0), "xd": (P * I, torch.float16, 0),
             "z": (P * max(2 * self.S * I, D), torch.float32, 0), "y": (P * D, torch.float32, 0),
-            "logits": (rows * (E + 1), torch.float32, 0), "route_counter": (1, torch.int32, 0),
+            "logits": (rows * (E + 1), torch.float32, 0), "route_counter": (3, torch.int32, 0),
             "pick": (P, torch.int32, 0), "wts": (P, torch.float32, 0), "ids": (maxu, torch.int32, 0),
             "count": (1, torch.int32, 0), "members": (maxu * rows, torch.int32, -1),
             "cnt_gu": (maxu * (I // 128) + 1, torch.int32, 0), "cnt_d": (rows * (D // 128) + 1, torch.int32, 0),
@@ -140,6 +140,7 @@ class Scratch:
             setattr(self, name, torch.full((max(n, 1),), v, dtype=dtype, device=device))
         self.xg, self.xu, self.y = self.xg.view(P, D), self.xu.view(P, D), self.y.view(P, D)
         self.xd = self.xd.view(P, I)
+        self.rotated = False    # route() also wrote xg / xu for its rows (the routing launch did rot_in's work)
 
     def window(self, R: int):
         """(ids, members [maxu, R]) of a call with R rows: the grouping's layout depends on R."""
@@ -165,13 +166,16 @@ def _fits(R: int, slots: int, s: Scratch):
 
 def route(x: torch.Tensor, gate: torch.Tensor, k: int, L: Layer, s: Scratch):
     """Fused routing of x [R, D] with router weight gate [E_routed, D] into the scratch (pick, wts, ids, count,
-    members), the shared expert as slot k when the layer has one; routed2(..., pick=None) runs the experts."""
+    members), the shared expert as slot k when the layer has one, and in the same launch the experts' input rotation
+    (rot_in's xg / xu); routed2(x, pick=None) then runs the experts on the same x."""
     R = x.shape[0]
     _fits(R, k + (L.shared_id >= 0), s)
     ids, members = s.window(R)
     n = R * s.slots
-    ext().route_group(x, gate, L.gate_w, k, L.shared_id, s.logits, s.route_counter, s.pick[:n], s.wts[:n], ids,
-                      s.count, members)
+    e = ext()
+    e.route_group(x, gate, L.gate_w, k, L.shared_id, s.logits, s.route_counter, s.pick[:n], s.wts[:n], ids, s.count,
+                  members, rotate=(L.gate.suh, L.up.suh, s.xg, s.xu, L.E))
+    s.rotated = True
 
 
 def routed2(x: torch.Tensor, pick: torch.Tensor | None, wts: torch.Tensor | None, L: Layer, s: Scratch,
@@ -191,7 +195,9 @@ def routed2(x: torch.Tensor, pick: torch.Tensor | None, wts: torch.Tensor | None
     pk, wt = s.pick[:P], s.wts[:P]
     if pick is not None:
         e.group_shared(pick, wts, x, x.stride(0), L.gate_w, L.shared_id, pk, wt, ids, s.count, members, R, k, L.E)
-    e.rot_in(x, x.stride(0), pk, L.gate.suh, L.up.suh, s.xg, s.xu, R, L.D, slots, L.E)
+    if pick is not None or not s.rotated:
+        e.rot_in(x, x.stride(0), pk, L.gate.suh, L.up.suh, s.xg, s.xu, R, L.D, slots, L.E)
+    s.rotated = False
     out = out if out is not None else torch.empty((R, L.D), dtype=x.dtype, device=x.device)
     if has_shared and out_shared is None:
         out_shared = torch.empty((R, L.D), dtype=x.dtype, device=x.device)
