@@ -694,7 +694,10 @@ def decoder_bench(dev, steps: int, warmup: int, dist, peak: float) -> dict:
         pt.capture()
         split[f"{part}_ms"] = time_steps(pt, steps, warmup, dist, dev)
         pt.graph = None
-    split["torch_standins_ms"] = res["1"]["ms_per_step"] - sum(split.values())
+    product_ms = sum(split.values())
+    split["torch_standins_ms"] = res["1"]["ms_per_step"] - product_ms
+    split["product_ms"] = product_ms
+    split["product_tok_s"] = 1.0 / (product_ms * 1e-3)      # this library's kernels alone, batch 1
     gbs = step_bytes / (res["1"]["ms_per_step"] * 1e-3) / 1e9
     return {"workload": "BASELINE configs[4]: 40-layer synthetic decoder (config-2 projections around stand-in mixer "
                         "cores, config-3 MoE in every layer, 6-bit mcg LM head to 248320, bf16 embedding), one decode "
