@@ -314,15 +314,18 @@ def moe_bench(dev, layers: int, steps: int, warmup: int, dist, peak: float, rank
             entry["weight_gbs_note"] = ("bytes the rank's rows pick on one GPU over the slowest rank's time; each "
                                         "rank reads only its own experts' share")
         res[str(R)] = entry
-    how = (f"fused routing, rot_in and {'one fused expert launch' if one else 'two fused expert launches'} a layer"
-           if world == 1 else
-           f"expert parallel over {world} GPUs: local routing, NCCL all_to_all dispatch of rows and picks, local "
-           f"experts, all_to_all of per-slot rows back, slot-ordered combine")
+    from vllm_espalier_b200._env import EP_EXCHANGE
+    exch = ("peer stores of rows and picks into the owners' inboxes (CUDA IPC, release/acquire flags), local "
+            "experts, peer stores of per-slot rows back to their home ranks" if EP_EXCHANGE == "p2p" else
+            "NCCL all_to_all dispatch of rows and picks, local experts, all_to_all of per-slot rows back")
+    how = (f"routing with the experts' input rotation fused, then "
+           f"{'one fused expert launch' if one else 'two fused expert launches'} a layer"
+           if world == 1 else f"expert parallel over {world} GPUs: local routing, {exch}, slot-ordered combine")
     return {"workload": f"BASELINE configs[2]: {layers} MoE layers a step, each with its own experts and router "
                         f"(256 experts 1/2/3-bit E2M1/int5, int6 shared, top-8), {how}, graph replay; at batch 1 the "
                         f"step touches more than the L2 holds",
             "layers": layers, "world": world, "scaling": "weak (R rows a rank)" if world > 1 else None,
-            "launches_per_layer": (3 if one else 4) if world == 1 else None, "batches": res}
+            "launches_per_layer": (2 if one else 3) if world == 1 else None, "batches": res}
 
 
 # ---------------------------------------------------------------------------------------------------------------

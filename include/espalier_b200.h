@@ -82,8 +82,10 @@ typedef struct esp_matrix {
  * rotation). x: [m][k] of x_dtype with row stride x_stride elements; y: [m][*] of y_dtype, row stride y_stride.
  * Scratch (caller-owned, never resized here):
  *   xh       fp16, at least esp_dense_xh_bytes(m, k, n_mats) bytes (rotated activations)
- *   z        fp32, at least esp_dense_z_bytes(m) bytes (split-K partial sums)
- *   counters int32, at least sum(n_s)/128 entries, zero before the first call and left zero by every call.
+ *   z        at least esp_dense_z_bytes(m) bytes, 16-byte aligned (split-K partial sums as tagged 8-byte words),
+ *            zero before the first call and left zero by every call that completes (after a call whose device status
+ *            is ESP_ERR_TIMEOUT, zero it again)
+ *   counters int32, at least sum(n_s)/128 entries, zero (the reference's argument; this kernel does not write it).
  * Results are row-invariant (a row's bits never depend on the other rows) and deterministic.
  * Replaces ext().dense(x, T[], suh[], svh[], col0[], y, xh, Z, counters, k2, cb, SK, W, PF, rot_smem)
  *                                              (vllm_espalier/csrc/experts.cpp:193-211, dense.cu:276-340).
@@ -279,20 +281,22 @@ int esp_wait_flag(const int* flag, int need, int* result, void* stream);
  * by the host (any collective) and esp_ipc_open maps another rank's inboxes into this process (no multicast object);
  * esp_ipc_close / esp_ipc_free undo them. Inboxes of a rank: x rows [world][R][D] (x's dtype), picks int32
  * [world][R][slots], y fp32 [R][slots][D], flags_x and flags_y int32 [world]; plus a local epoch word and counters,
- * zero at allocation. Every rank calls with the same R, slots and world; the calls of a layer are, in order:
+ * zero at allocation. Every rank calls with the same R, slots and world; a layer is the routing (esp_route_group of
+ * this rank's rows, global ids), then:
  *
- *   esp_ep_dispatch  x [R][D] (row stride x_stride) and pick [R][slots] (global ids, the shared slot last) of this
- *                    rank's rows: each row to the ranks that own one of its routed picks, every pick row to every
- *                    rank; inbox_x / inbox_pick / flags_x: host arrays of every rank's inbox bases (this rank's own
- *                    included)
- *   esp_ep_recv      waits for every source's flag, writes local_pick int32 [world][R][slots] (local expert ids, the
- *                    local shared entry for this rank's own shared slots, -1 elsewhere) for esp_group / esp_rot_in /
- *                    the expert kernels
- *   esp_ep_return    y fp32 [world][R][slots][D] (the expert kernels' per-slot output): each locally computed slot's
- *                    row to its home rank's inbox (inbox_y / flags_y: host arrays of every rank's bases); done: int32
- *                    [world] counters, zero, left zero
- *   esp_ep_finish    waits for every owner's flag, then out / out_shared [R][D] as esp_ep_combine (slot-ordered fp32
- *                    fused multiply-adds; bit-identical to one GPU); advances *epoch; count: an int32 counter
+ *   esp_ep_in   x [R][D] (row stride x_stride) and pick [R][slots] (global ids, the shared slot last) of this rank's
+ *               rows: each row to the ranks that own one of its routed picks (and to its own rank, which computes its
+ *               shared slot), every pick row to every rank (inbox_x / inbox_pick / flags_x: host arrays of every
+ *               rank's inbox bases, this rank's own included); then, once every source's flag is seen, local_pick
+ *               int32 [world][R][slots] (local expert ids, the local shared entry nl for this rank's own shared
+ *               slots, -1 elsewhere), its grouping (uids / ucount / members as esp_group with maxm <= 32), and the
+ *               received rows' rotation for the experts (xg / xu [world R slots][D] fp16, as esp_rot_in with the
+ *               stacked suh of the local table's nl + 1 entries); counter: 2 int32 words, zero, left zero
+ *   the expert layer (esp_moe_layer with n_routed = 0 over world * R rows: y fp32 [world][R][slots][D])
+ *   esp_ep_out  each locally computed slot's y row to its home rank's inbox (inbox_y / flags_y: host arrays of
+ *               every rank's bases; done: int32 [world], zero, left zero), then, once every owner's flag is seen,
+ *               out / out_shared [R][D] as esp_ep_combine (slot-ordered fp32 fused multiply-adds; bit-identical to
+ *               one GPU); advances *epoch; count: an int32 counter, zero, left zero
  *
  * Waits give up after 0.2 s and record ESP_ERR_TIMEOUT (esp_device_status). The epoch lives on the device, so a
  * CUDA graph of the layer replays correctly.
@@ -302,16 +306,13 @@ int esp_ipc_alloc(size_t bytes, void** ptr, void* handle);
 int esp_ipc_open(const void* handle, void** ptr);
 int esp_ipc_close(void* ptr);
 int esp_ipc_free(void* ptr);
-int esp_ep_dispatch(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots,
-                    int n_routed, int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick,
-                    int* const* flags_x, const int* epoch, void* stream);
-int esp_ep_recv(const int* inbox_pick, const int* flags_x, const int* epoch, int world, int rank, int R, int slots,
-                int n_routed, int E, int* local_pick, void* stream);
-int esp_ep_return(const float* y, const int* local_pick, int world, int rank, int R, int slots, int D,
-                  float* const* inbox_y, int* const* flags_y, const int* epoch, int* done, void* stream);
-int esp_ep_finish(const float* inbox_y, const int* flags_y, const int* pick, const float* wts, void* out,
-                  void* out_shared, int out_dtype, int R, int D, int slots, int n_routed, int E, int world, int* epoch,
-                  int* count, void* stream);
+int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots, int n_routed,
+              int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick, int* const* flags_x,
+              const int* epoch, int* local_pick, int* uids, int* ucount, int* members, int maxm, int maxu,
+              const void* suh_gate, const void* suh_up, void* xg, void* xu, int* counter, void* stream);
+int esp_ep_out(const float* y, const int* local_pick, int world, int rank, int R, int slots, int n_routed, int E,
+               int D, float* const* inbox_y, int* const* flags_y, const int* pick, const float* wts, void* out,
+               void* out_shared, int out_dtype, int* epoch, int* done, int* count, void* stream);
 
 #ifdef __cplusplus
 }

@@ -143,7 +143,9 @@ def test_merged_equals_alone(dev):
         c += m.out_features
 
 
-def test_graph_equals_eager_and_counters_zero(dev):
+def test_graph_equals_eager_and_scratch_zero(dev):
+    """Graph replay gives the eager bits, and the scratch the kernel shares between launches (the tagged split-K
+    partials, the counters) is left zero by every launch."""
     ms, x, _ = _layer("int6_single", 512, [256], 7, 8, 8, "bf16", dev)
     d = D.Dense(ms)
     eager = d.forward(x).clone()
@@ -162,6 +164,7 @@ def test_graph_equals_eager_and_counters_zero(dev):
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
     assert int(d.ws.counters.abs().sum()) == 0
+    assert not bool(d.ws.z.view(torch.int32).any())
 
 
 def test_fp32_and_fp16_io(dev):

@@ -67,10 +67,9 @@ SIGNATURES = {
     "esp_ipc_open": (I, [P, C.POINTER(P)]),
     "esp_ipc_close": (I, [P]),
     "esp_ipc_free": (I, [P]),
-    "esp_ep_dispatch": (I, [P, I, L, I, I, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), C.POINTER(P), P, P]),
-    "esp_ep_recv": (I, [P, P, P, I, I, I, I, I, I, P, P]),
-    "esp_ep_return": (I, [P, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), P, P, P]),
-    "esp_ep_finish": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P]),
+    "esp_ep_in": (I, [P, I, L, I, I, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), C.POINTER(P), P, P, P, P, P, I, I,
+                      P, P, P, P, P, P]),
+    "esp_ep_out": (I, [P, P, I, I, I, I, I, I, I, C.POINTER(P), C.POINTER(P), P, P, P, P, I, P, P, P, P]),
 }
 
 

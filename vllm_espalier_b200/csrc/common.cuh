@@ -164,6 +164,15 @@ __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
     asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Tagged 64-bit words (value bits in the low half, a nonzero tag in the high half): each word is written and read
+// whole (single-copy atomic at GPU scope), so a reader that sees the tag sees the value, with no fence on either side.
+__device__ __forceinline__ void st_relaxed_v2_u64(void* p, uint64_t a, uint64_t b) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_relaxed_v2_u64(const void* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // Thread-block cluster: this CTA's rank, a barrier of every thread of the cluster (release / acquire, so shared
 // memory written before it is visible to the other CTAs' reads after it), and loads from another CTA's shared memory.
 __device__ __forceinline__ uint32_t cluster_rank() {

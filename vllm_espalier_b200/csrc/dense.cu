@@ -18,15 +18,21 @@
 //     unit measured ~40 ns of TMA issue each, too slow for 1 KB units). 16 consumer warps in two groups (alternate
 //     units) decode tile w of every unit straight into the A fragment of mma.sync m16n8k16 (M = 16 output columns,
 //     N = 8 tokens), i.e. each weight is decoded once whatever the number of rows.
-//   * A block whose k range spans several CTAs' ranges is finished by the last of them to arrive (one acq_rel atomic
-//     a CTA and block), which adds their partial sums in CTA (= k) order; a block inside one CTA's range is finished in
-//     place. A CTA's range meets at most two partial blocks (its first and its last), stored in partial slots 2c and
-//     2c + 1. Finishing = FWHT-128 of the sums, * step, * H/sqrt(128) * svh, in the reference's order, then the store
-//     in y's dtype. The ranges depend on the shape and the SM count only.
+//   * A block whose k range spans several CTAs' ranges is finished by the CTA holding its first k-tile (for which it is
+//     the last segment); every other CTA of the block holds it as its first segment and stores that partial, as
+//     tagged 64-bit words (value | 1 << 32), in its one slot of Z. The finisher reads the slots in CTA (= k) order,
+//     polling each word's tag (bounded), adds them after its own sums, and clears the slots to zero for the next
+//     launch: no fence, no atomic, and the other CTAs leave as soon as their stores are issued. A block inside one
+//     CTA's range is finished in place. Finishing = FWHT-128 of the sums, * step, * H/sqrt(128) * svh, in the
+//     reference's order, then the store in y's dtype. The ranges depend on the shape and the SM count only.
+//   * Decode ahead (fused path): the weights do not depend on the previous kernel, so a CTA decodes its units into
+//     shared memory before the launch wait while the previous launch drains; when every unit of every CTA fits, all
+//     of them are (the wait is then followed by the rotations, the products and the finishing alone).
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -90,13 +96,15 @@ struct DenseParams {
     void* y;
     int y_dtype;
     long long y_stride;
-    float* Z;                    // partial sums [2 * G][M][128]: slot 2c = CTA c's first block, 2c + 1 its last
-    int* counters;               // [blocks], zero on entry and on exit
+    uint64_t* Z;                 // tagged partial sums [G][M][128]: CTA c's first segment; zero on entry and exit
+    int* counters;               // [blocks], zero (the reference's argument; not written by this kernel)
     int M, Mp, K, KT, U, G;      // rows, padded rows, inputs, k tiles, units, CTAs (G <= U)
     int NB;                      // 128-column blocks
     int S;                       // > 1: the S CTAs of a block form a thread-block cluster (block-aligned k-slices)
     float scale;                 // codebook step of the kernel form
     int npre;                    // fused path: units decoded ahead of the launch wait (whole stages, one segment)
+    int ahead_all;               // fused path: every CTA decodes all of its units ahead of the wait (npre = max)
+    int stages;                  // ring depth in stages (<= STAGES)
 };
 
 struct RotParams {
@@ -167,6 +175,26 @@ __device__ __forceinline__ int shard_of(int bg, const DenseParams& p) {
     return s;
 }
 
+// Tagged partial sums: TAG marks a word written by the launch in flight; a consumed slot is cleared to zero.
+constexpr uint64_t TAG = 1ull << 32;
+// Poll 4 tagged words until all carry the tag; gives up after WAIT_NS (recording ESP_ERR_TIMEOUT, values then 0).
+__device__ __forceinline__ float4 poll_tagged4(const uint64_t* w) {
+    const uint64_t t0 = global_ns();
+    while (true) {
+        uint64_t a, b, c, d;
+        ld_relaxed_v2_u64(w, a, b);
+        ld_relaxed_v2_u64(w + 2, c, d);
+        if (((a & b & c & d) >> 32) != 0)
+            return make_float4(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b), __uint_as_float((uint32_t)c),
+                               __uint_as_float((uint32_t)d));
+        const uint64_t dt = global_ns() - t0;
+        if (dt > WAIT_NS || (dt > 20000 && *reinterpret_cast<volatile int*>(&g_device_status) == ESP_ERR_TIMEOUT)) {
+            report(ESP_ERR_TIMEOUT);
+            return make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
 // fp16 H(x[row] * suh) / sqrt(128) of 128-input chunks, stored as MMA B-fragment slices (k-tile, k-half, row, 8): the
 // rot_kernel arithmetic (bit-identical), by one warp into shared memory. Items it = row + MP * chunk_offset; the warp's
 // items are loaded in batches of RB before their transforms so the global-load latency is paid once a batch.
@@ -216,12 +244,11 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
     constexpr int STAGE_W = UPS * (UNIT_W + (FUSED ? 0 : SLICE_W));
     constexpr bool BULKW = FUSED && BULK;
     extern __shared__ __align__(128) uint32_t smem[];
-    float* red = reinterpret_cast<float*>(smem + (size_t)STAGES * STAGE_W);   // [MP][RED_STRIDE]
+    float* red = reinterpret_cast<float*>(smem + (size_t)p.stages * STAGE_W);   // [MP][RED_STRIDE]
     uint32_t* xrot = reinterpret_cast<uint32_t*>(red + MP * RED_STRIDE);      // fused: [chunks][8][2][MP][4]
     uint4* pre = reinterpret_cast<uint4*>(xrot + (FUSED ? (size_t)p.xh_chunks * 8 * SLICE_W : 0));  // [npre][8][32]
     uint64_t* full = reinterpret_cast<uint64_t*>(pre + (FUSED ? (size_t)p.npre * 8 * 32 : 0));
     uint64_t* empty = full + STAGES;
-    __shared__ int s_lastv[2];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
@@ -297,7 +324,7 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
             }
         };
         Cur cur = start();
-        const int pre = min(nst, STAGES);
+        const int pre = min(nst, p.stages);
         if constexpr (FUSED) {
             for (int i = 0; i < pre; ++i) {
                 fill(i, i, true, false, cur);
@@ -313,11 +340,11 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                 cp_async_arrive(&full[i]);
             }
         }
-        for (int i = STAGES, slot = 0, phase = 0; i < nst; ++i) {
+        for (int i = p.stages, slot = 0, phase = 0; i < nst; ++i) {
             if (!mbar_wait(&empty[slot], phase)) break;   // gave up (status recorded)
             fill(i, slot, true, !FUSED, cur);
             if (!BULKW) cp_async_arrive(&full[slot]);
-            if (++slot == STAGES) {
+            if (++slot == p.stages) {
                 slot = 0;
                 phase ^= 1;
             }
@@ -340,11 +367,16 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
             for (int i = threadIdx.x; i < words; i += CT) xrot[i] = 0u;
             named_sync(1, CT);
         }
-        int pend_bg[2], npend = 0;     // blocks whose partial sums this CTA wrote, completed after the last segment
         int bg = bg0, kt = kt0, li = 0, j = 0, slot = 0, phase = 0;
         bool from_zero = kt0 == 0;     // the current segment starts at the block's first k-tile
         int chunk0 = 0;                // fused: first 128-input chunk held in xrot
         bool seg_start = true;
+        auto advance = [&]() {
+            if (++slot == p.stages) {
+                slot = 0;
+                phase ^= 1;
+            }
+        };
         auto rotate_segment = [&]() {  // rotate the current segment's inputs (from unit li on) into shared memory
             const int seg_kt1 = min(p.KT, kt + (n - li));
             chunk0 = kt >> 3;
@@ -353,96 +385,11 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
             named_sync(1, CT);
             seg_start = false;
         };
-        if constexpr (FUSED) {
-            // Decode ahead: the weights are not the previous kernel's output, so the first npre units (whole stages
-            // of this CTA's one segment) are decoded into shared memory before the wait on that kernel, while this
-            // CTA would otherwise sit idle; their products follow the wait in the loop's own order and accumulators,
-            // so the sums are the bits the loop would give.
-            for (int sidx = 0; sidx < p.npre / UPS; ++sidx) {
-                mbar_wait(&full[slot], phase);
-                const uint32_t* st = smem + (size_t)slot * STAGE_W;
-    #pragma unroll
-                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
-                    const int jj = j2 * GROUPS + grp;
-                    uint32_t a[4];
-                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
-                    pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane] = make_uint4(a[0], a[1], a[2], a[3]);
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-                if (++slot == STAGES) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-            }
-        }
-        pdl_wait();
-        if constexpr (FUSED) {
-            if (p.npre) {
-                rotate_segment();
-                for (int sidx = 0; sidx < p.npre / UPS; ++sidx) {
-    #pragma unroll
-                    for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
-                        const int jj = j2 * GROUPS + grp;
-                        const uint4 v = pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane];
-                        const uint32_t a[4] = {v.x, v.y, v.z, v.w};
-                        const uint32_t* xs = xrot + (size_t)(kt + sidx * UPS + jj - 8 * chunk0) * SLICE_W;
-    #pragma unroll
-                        for (int q = 0; q < NTG; ++q)
-                            mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
-                    }
-                }
-                kt += p.npre;
-                li = p.npre;
-            }
-        }
-        while (li < n) {
-            if (FUSED && seg_start) rotate_segment();   // rotate this segment's inputs into shared memory
-            if (j == 0) mbar_wait(&full[slot], phase);
-            const uint32_t* st = smem + (size_t)slot * STAGE_W;
-            const int stage_n = min(UPS, n - (li - j));
-            const int run_end = min(stage_n, j + (p.KT - kt));
-            const int kt_at_j = kt;
-            auto slice = [&](int jj) -> const uint32_t* {
-                if constexpr (FUSED) return xrot + (size_t)(kt_at_j + jj - j - 8 * chunk0) * SLICE_W;
-                else return st + UPS * UNIT_W + jj * SLICE_W;
-            };
-            if (j == 0 && run_end == UPS) {      // the common case: a whole stage inside one segment
-    #pragma unroll
-                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
-                    const int jj = j2 * GROUPS + grp;
-                    uint32_t a[4];
-                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
-                    const uint32_t* xs = slice(jj);
-    #pragma unroll
-                    for (int q = 0; q < NTG; ++q)
-                        mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
-                }
-            } else {
-                for (int jj = j; jj < run_end; ++jj) {
-                    if (GROUPS > 1 && (jj % GROUPS) != grp) continue;
-                    uint32_t a[4];
-                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
-                    const uint32_t* xs = slice(jj);
-    #pragma unroll
-                    for (int q = 0; q < NTG; ++q) mma16816(acc[0][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
-                }
-            }
-            kt += run_end - j;
-            li += run_end - j;
-            j = run_end;
-            if (j == stage_n) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-                j = 0;
-                if (++slot == STAGES) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-            }
-            if (kt != p.KT && li != n) continue;
-
-            // ---- segment end: this warp's 16 columns (even + odd sums) into red[token][column] ----
+        // Segment end: this warp's 16 columns (even + odd sums) into red[token][column], then by the segment's place
+        // in its block: the whole block (finish in place), a later k-slice (store the tagged partial: it is this
+        // CTA's first segment), or the block's first k-slice with the block running on past this CTA's range (the
+        // finisher: its last segment).
+        auto segment_end = [&]() {
             const int col = wl * 16 + g;
     #pragma unroll
             for (int gi = 0; gi < GROUPS; ++gi) {     // group 0's sums, then group 1's added, in that order
@@ -468,9 +415,9 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                 for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
             named_sync(1, CT);
 
+            const DShard& S = p.s[shard_of(bg, p)];
+            const int bl = bg - S.nb0;
             if (from_zero && kt == p.KT) {   // this CTA owns the whole block: finish it now
-                const DShard& S = p.s[shard_of(bg, p)];
-                const int bl = bg - S.nb0;
                 const uint2 sv = load_svh(S, bl, lane);
                 for (int r = warp; r < p.M; r += CWARPS) {
                     const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
@@ -478,12 +425,46 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                     finish_store(v, lane, S, bl, r, p, sv);
                 }
             } else if (p.S > 1) {            // partial of a clustered block: stays in red, added after the loop
-            } else {                         // partial: store it; the arrival on the block's counter waits for the end
-                float* zs = p.Z + (size_t)(2 * c + (bg == bg0 ? 0 : 1)) * p.M * 128;   // first / last block's slot
-                for (int r = warp; r < p.M; r += CWARPS)
-                    *reinterpret_cast<float4*>(zs + r * 128 + 4 * lane) =
-                        *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-                pend_bg[npend++] = bg;
+            } else if (!from_zero) {         // a later k-slice: publish the partial, tagged, in this CTA's slot
+                uint64_t* zs = p.Z + (size_t)c * p.M * 128;
+                for (int r = warp; r < p.M; r += CWARPS) {
+                    const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+                    uint64_t* w = zs + r * 128 + 4 * lane;
+                    st_relaxed_v2_u64(w, TAG | __float_as_uint(q.x), TAG | __float_as_uint(q.y));
+                    st_relaxed_v2_u64(w + 2, TAG | __float_as_uint(q.z), TAG | __float_as_uint(q.w));
+                }
+            } else {                         // the finisher: add the later k-slices' partials in k order
+                const int c_hi = cta_of(bg * p.KT + p.KT - 1, p);
+                const uint2 sv = load_svh(S, bl, lane);
+                for (int r = warp; r < p.M; r += CWARPS) {
+                    const float4 own = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+                    float v[4] = {0.f + own.x, 0.f + own.y, 0.f + own.z, 0.f + own.w};
+                    for (int c4 = c + 1; c4 <= c_hi; c4 += 4) {   // 4 slots' reads in flight, then added in order
+                        float4 f[4];
+                        uint32_t ok = 0;
+    #pragma unroll
+                        for (int d = 0; d < 4; ++d)
+                            if (c4 + d <= c_hi) {
+                                const uint64_t* w = p.Z + ((size_t)(c4 + d) * p.M + r) * 128 + 4 * lane;
+                                uint64_t a, b, cc, dd;
+                                ld_relaxed_v2_u64(w, a, b);
+                                ld_relaxed_v2_u64(w + 2, cc, dd);
+                                f[d] = make_float4(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b),
+                                                   __uint_as_float((uint32_t)cc), __uint_as_float((uint32_t)dd));
+                                ok |= (((a & b & cc & dd) >> 32) != 0 ? 1u : 0u) << d;
+                            }
+    #pragma unroll
+                        for (int d = 0; d < 4; ++d)
+                            if (c4 + d <= c_hi) {
+                                uint64_t* w = p.Z + ((size_t)(c4 + d) * p.M + r) * 128 + 4 * lane;
+                                if (!((ok >> d) & 1u)) f[d] = poll_tagged4(w);
+                                v[0] += f[d].x; v[1] += f[d].y; v[2] += f[d].z; v[3] += f[d].w;
+                                st_relaxed_v2_u64(w, 0ull, 0ull);       // the slot is empty again
+                                st_relaxed_v2_u64(w + 2, 0ull, 0ull);
+                            }
+                    }
+                    finish_store(v, lane, S, bl, r, p, sv);
+                }
             }
             named_sync(1, CT);   // red (and the rotation buffer) are reused by the next segment
             if (kt == p.KT) {
@@ -492,50 +473,107 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                 from_zero = true;
             }
             seg_start = true;
-        }
+        };
 
-        if (npend) {
-            named_sync(1, CT);                 // every partial of this CTA is stored
-            if (threadIdx.x < npend) {
-                const int b = pend_bg[threadIdx.x];
-                const int nc = cta_of(b * p.KT + p.KT - 1, p) - cta_of(b * p.KT, p) + 1;
-                s_lastv[threadIdx.x] = arrive_acq_rel(&p.counters[b]) == nc - 1;   // publishes / sees the partials
-            }
-            named_sync(1, CT);
-            for (int pi = 0; pi < npend; ++pi) {
-                if (!s_lastv[pi]) continue;
-                const int b = pend_bg[pi];
-                const DShard& S = p.s[shard_of(b, p)];
-                const int bl = b - S.nb0;
-                const uint2 sv = load_svh(S, bl, lane);
-                // the block's CTAs, added in k order; only the first can hold it as its last block (slot 2c + 1)
-                const int c_lo = cta_of(b * p.KT, p), c_hi = cta_of(b * p.KT + p.KT - 1, p);
-                const int lo_slot = 2 * c_lo + (range_start(c_lo, p) < b * p.KT ? 1 : 0);
-                for (int r = warp; r < p.M; r += CWARPS) {
-                    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int c8 = c_lo; c8 <= c_hi; c8 += 8) {
-                        float4 q[8];
+        // Decode ahead: the weights are not the previous kernel's output, so units are decoded into shared memory
+        // (pre) before the wait on that kernel, while this CTA would otherwise sit idle: all of them (ahead_all), or
+        // the first npre (whole stages of this CTA's one segment). Their products follow the wait in the loop's own
+        // order and accumulators, so the sums are the bits the loop gives without decoding ahead.
+        const bool ah = FUSED && p.ahead_all;
+        if constexpr (FUSED) {
+            const int nahead = ah ? nst : p.npre / UPS;
+            for (int sidx = 0; sidx < nahead; ++sidx) {
+                mbar_wait(&full[slot], phase);
+                const uint32_t* st = smem + (size_t)slot * STAGE_W;
+                const int m = min(UPS, n - sidx * UPS);
     #pragma unroll
-                        for (int d = 0; d < 8; ++d) {
-                            const int cc = c8 + d;
-                            const int slot = cc == c_lo ? lo_slot : 2 * cc;
-                            q[d] = cc <= c_hi ? __ldcg(reinterpret_cast<const float4*>(p.Z + ((size_t)slot * p.M + r) * 128 +
-                                                                                       4 * lane))
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-    #pragma unroll
-                        for (int d = 0; d < 8; ++d)
-                            if (c8 + d <= c_hi) {
-                                sum.x += q[d].x; sum.y += q[d].y; sum.z += q[d].z; sum.w += q[d].w;
-                            }
+                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                    const int jj = j2 * GROUPS + grp;
+                    if (jj < m) {
+                        uint32_t a[4];
+                        decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                        pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane] = make_uint4(a[0], a[1], a[2], a[3]);
                     }
-                    float v[4] = {sum.x, sum.y, sum.z, sum.w};
-                    finish_store(v, lane, S, bl, r, p, sv);
                 }
-                if (threadIdx.x == 0) p.counters[b] = 0;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                advance();
             }
         }
-
+        pdl_wait();
+        if constexpr (FUSED) {
+            if (!ah && p.npre) {
+                rotate_segment();
+                for (int sidx = 0; sidx < p.npre / UPS; ++sidx) {
+    #pragma unroll
+                    for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                        const int jj = j2 * GROUPS + grp;
+                        const uint4 v = pre[((sidx * UPS + jj) * 8 + wl) * 32 + lane];
+                        const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+                        const uint32_t* xs = xrot + (size_t)(kt + sidx * UPS + jj - 8 * chunk0) * SLICE_W;
+    #pragma unroll
+                        for (int q = 0; q < NTG; ++q)
+                            mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                    }
+                }
+                kt += p.npre;
+                li = p.npre;
+            }
+        }
+        while (li < n) {
+            if (FUSED && seg_start) rotate_segment();   // rotate this segment's inputs into shared memory
+            if (j == 0 && !ah) mbar_wait(&full[slot], phase);
+            const uint32_t* st = smem + (size_t)slot * STAGE_W;
+            const int stage_n = min(UPS, n - (li - j));
+            const int run_end = min(stage_n, j + (p.KT - kt));
+            const int kt_at_j = kt, u_at_0 = li - j;   // u_at_0: this stage's first unit in the CTA's range
+            auto slice = [&](int jj) -> const uint32_t* {
+                if constexpr (FUSED) return xrot + (size_t)(kt_at_j + jj - j - 8 * chunk0) * SLICE_W;
+                else return st + UPS * UNIT_W + jj * SLICE_W;
+            };
+            auto tile = [&](int jj, uint32_t (&a)[4]) {   // unit jj of the stage: decoded ahead, or decoded now
+                if (ah) {
+                    const uint4 v = pre[((u_at_0 + jj) * 8 + wl) * 32 + lane];
+                    a[0] = v.x; a[1] = v.y; a[2] = v.z; a[3] = v.w;
+                } else {
+                    decode_a<CB, K>(st + jj * UNIT_W + wl * TW, lane, a);
+                }
+            };
+            if (j == 0 && run_end == UPS) {      // the common case: a whole stage inside one segment
+    #pragma unroll
+                for (int j2 = 0; j2 < UPS / GROUPS; ++j2) {
+                    const int jj = j2 * GROUPS + grp;
+                    uint32_t a[4];
+                    tile(jj, a);
+                    const uint32_t* xs = slice(jj);
+    #pragma unroll
+                    for (int q = 0; q < NTG; ++q)
+                        mma16816(acc[j2 & 1][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                }
+            } else {
+                for (int jj = j; jj < run_end; ++jj) {
+                    if (GROUPS > 1 && (jj % GROUPS) != grp) continue;
+                    uint32_t a[4];
+                    tile(jj, a);
+                    const uint32_t* xs = slice(jj);
+    #pragma unroll
+                    for (int q = 0; q < NTG; ++q) mma16816(acc[0][q], a, xs[(8 * q + g) * 4 + t], xs[(MP + 8 * q + g) * 4 + t]);
+                }
+            }
+            kt += run_end - j;
+            li += run_end - j;
+            j = run_end;
+            if (j == stage_n) {
+                if (!ah) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                    advance();
+                }
+                j = 0;
+            }
+            if (kt != p.KT && li != n) continue;
+            segment_end();
+        }
     }
 
     if (p.S > 1) {   // the block's S CTAs (one cluster, rank = k-slice) add their partials in rank order
@@ -610,9 +648,9 @@ __global__ void __launch_bounds__(128) had_kernel(const __half* __restrict__ x, 
     store4(y, F16, i, v);
 }
 
-size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks, int npre) {
+size_t dense_smem_bytes(int K, int ntg, bool fused, int chunks, int npre, int stages = STAGES) {
     const int tw = 8 * K, unit_w = 8 * tw, slice_w = 8 * ntg * 8;
-    return (size_t)STAGES * UPS * (unit_w + (fused ? 0 : slice_w)) * 4 + (size_t)8 * ntg * RED_STRIDE * 4 +
+    return (size_t)stages * UPS * (unit_w + (fused ? 0 : slice_w)) * 4 + (size_t)8 * ntg * RED_STRIDE * 4 +
            (fused ? (size_t)chunks * 8 * slice_w * 4 + (size_t)npre * 8 * 32 * 16 : 0) + 2 * STAGES * 8;
 }
 
@@ -624,6 +662,17 @@ bool ahead_enabled() {
     static const bool on = [] {
         const char* v = std::getenv("ESPALIER_DENSE_AHEAD");
         return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// With fewer blocks than SMs, ESPALIER_DENSE_SPLIT=slices gives every block S = SMs / blocks equal k-slices (one
+// segment a CTA, G = blocks * S CTAs); the default, ranges, splits the units in one equal range an SM (every SM busy,
+// a CTA meeting at most two blocks), used when every CTA's units fit the shared memory decoded.
+bool split_ranges() {
+    static const bool on = [] {
+        const char* v = std::getenv("ESPALIER_DENSE_SPLIT");
+        return !(v && std::strcmp(v, "slices") == 0);
     }();
     return on;
 }
@@ -643,7 +692,7 @@ bool cluster_enabled() {
 template <int CB, int K, int NTG, bool FUSED>
 int launch_dense(DenseParams p, void* stream) {
     auto kern = dense_kernel<CB, K, NTG, FUSED>;
-    const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks, FUSED ? p.npre : 0);
+    const size_t smem = dense_smem_bytes(K, NTG, FUSED, p.xh_chunks, FUSED ? p.npre : 0, p.stages);
     static size_t opted = 0;
     if (smem > opted) {
         if (int rc = allow_smem(kern, FUSED ? SMEM_LIMIT : smem)) return rc;
@@ -684,15 +733,14 @@ int launch_dense(DenseParams p, void* stream) {
 
 template <int CB, int K>
 int launch_dense_ntg(const DenseParams& p, bool fused, void* stream) {
-#define ESP_NTG(N_) \
-    return fused ? launch_dense<CB, K, N_, true>(p, stream) : launch_dense<CB, K, N_, false>(p, stream);
+    // the fused path is planned for one token group only (up to 8 rows)
+    if (fused) return p.Mp == 8 ? launch_dense<CB, K, 1, true>(p, stream) : ESP_ERR_INVALID;
     switch (p.Mp / 8) {
-        case 1: ESP_NTG(1)
-        case 2: ESP_NTG(2)
-        case 3: ESP_NTG(3)
-        default: ESP_NTG(4)
+        case 1: return launch_dense<CB, K, 1, false>(p, stream);
+        case 2: return launch_dense<CB, K, 2, false>(p, stream);
+        case 3: return launch_dense<CB, K, 3, false>(p, stream);
+        default: return launch_dense<CB, K, 4, false>(p, stream);
     }
-#undef ESP_NTG
 }
 
 // Everything esp_dense checks and derives on the host, before any device work.
@@ -753,38 +801,58 @@ int dense_plan(const void* x, int x_dtype, long long x_stride, int m, int k, con
     p.KT = k / 16;
     p.U = nbt * p.KT;
     p.NB = nbt;
-    // Fewer blocks than SMs: S CTAs a block, each an equal k-slice, so a CTA has one segment and a block S partials
-    // (stream-K ranges over all SMs balance the decode better but pay a mid-range segment switch and a second
-    // partial a CTA, which measured slower). Otherwise one range an SM over whole blocks, with at most a partial
-    // block at each end.
-    {
-        const int sms = device_sms() * CTAS_PER_SM;
-        p.G = nbt >= sms ? sms : nbt * std::min(sms / nbt, p.KT);
-    }
+    const int sms = device_sms() * CTAS_PER_SM;
+    // the fused path rotates each segment's inputs inside the kernel; a segment spans at most the CTA's units or one
+    // block's k-tiles, plus one chunk of misalignment
+    auto chunks_for = [&](int G) {
+        const long long per_cta = (p.U + G - 1) / G;
+        const int max_kt = (int)std::min<long long>(p.KT, per_cta);
+        return std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
+    };
+    // the deepest ring (down to 3 stages) beside all of a CTA's units decoded, or 0 if none fits
+    auto ahead_stages = [&](int G) {
+        const int nmax = (p.U + G - 1) / G;
+        for (int st = STAGES; st >= 3; --st)
+            if (dense_smem_bytes(K, 1, true, chunks_for(G), nmax, st) <= SMEM_LIMIT) return st;
+        return 0;
+    };
+    // Fewer blocks than SMs: one equal range of units an SM when every CTA's units fit the shared memory decoded
+    // (split_ranges; every SM busy, a CTA meeting at most two blocks), else S CTAs a block, each an equal k-slice (one
+    // segment a CTA, a block's S partials). Otherwise one range an SM over whole blocks, with at most a partial block
+    // at each end. The choice depends on the shape alone (not on the rows), so a row's bits do not depend on the
+    // others.
+    const bool few = nbt < sms;
+    p.G = few ? nbt * std::min(sms / nbt, p.KT) : sms;
+    if (few && split_ranges() && !cluster_enabled() && ahead_stages(std::min(sms, p.U))) p.G = std::min(sms, p.U);
     ESP_REQUIRE((long long)p.U * p.G < (1ll << 31), ESP_ERR_INVALID, "esp_dense: layer too large (%d units)", p.U);
     // k-slices of a block finish inside one thread-block cluster when there are 2..16 of them (the limit of a
     // non-portable cluster on this GPU)
-    p.S = (nbt < p.G && cluster_enabled() && p.G / nbt >= 2 && p.G / nbt <= 16) ? p.G / nbt : 0;
+    p.S = (few && p.G % nbt == 0 && cluster_enabled() && p.G / nbt >= 2 && p.G / nbt <= 16) ? p.G / nbt : 0;
     p.scale = cb_step(cb);
-    p.Z = z;
-    const size_t zneed = (size_t)2 * p.G * m * 128 * 4;
+    p.Z = reinterpret_cast<uint64_t*>(z);
+    const size_t zneed = (size_t)p.G * m * 128 * 8;
     ESP_REQUIRE((zneed == 0 || z) && z_bytes >= zneed && aligned(z, 16), ESP_ERR_SCRATCH,
                 "esp_dense: Z scratch needs %zu bytes, got %zu", zneed, z_bytes);
 
-    // the fused path rotates each segment's inputs inside the kernel; a segment spans at most the CTA's units or one
-    // block's k-tiles, plus one chunk of misalignment
-    const long long per_cta = (p.U + p.G - 1) / p.G;
-    const int max_kt = (int)std::min<long long>(p.KT, per_cta);
-    const int chunks = std::min(p.KT / 8, (max_kt + 7) / 8 + 1);
+    const int chunks = chunks_for(p.G);
     // up to 8 rows the in-kernel rotation is cheaper than a rotation launch; above, its loads serialise per row
     pl.fused = mp == 8 && dense_smem_bytes(K, mp / 8, true, chunks, 0) <= SMEM_LIMIT;
-    // decode ahead (fused path, one segment a CTA, i.e. fewer blocks than CTAs): as many whole stages as the shared
-    // memory beside the ring holds, leaving the loop at least one unit of every CTA (U / G is the smallest range)
+    // decode ahead (fused path, fewer blocks than CTAs): all of every CTA's units where they fit beside a ring of at
+    // least 3 stages, else (the slices) as many whole stages of the one segment as the shared memory beside the ring
+    // holds, leaving the loop at least one unit of every CTA (U / G is the smallest range)
     p.npre = 0;
-    if (pl.fused && ahead_enabled() && nbt < device_sms() * CTAS_PER_SM) {
-        const size_t base = dense_smem_bytes(K, 1, true, chunks, 0);
-        const int cap = base < SMEM_LIMIT ? (int)((SMEM_LIMIT - base) / (8 * 32 * 16)) : 0;
-        p.npre = std::max(0, std::min(cap, p.U / p.G - 1) / UPS * UPS);
+    p.ahead_all = 0;
+    p.stages = STAGES;
+    if (pl.fused && few && ahead_enabled()) {
+        if (const int st = p.S == 0 ? ahead_stages(p.G) : 0) {
+            p.stages = st;
+            p.ahead_all = 1;
+            p.npre = (p.U + p.G - 1) / p.G;
+        } else if (p.G % nbt == 0) {
+            const size_t base = dense_smem_bytes(K, 1, true, chunks, 0);
+            const int cap = base < SMEM_LIMIT ? (int)((SMEM_LIMIT - base) / (8 * 32 * 16)) : 0;
+            p.npre = std::max(0, std::min(cap, p.U / p.G - 1) / UPS * UPS);
+        }
     }
     p.x = x;
     p.x_dtype = x_dtype;
@@ -833,7 +901,7 @@ size_t esp_dense_xh_bytes(int m, int k, int n_mats) {
     return (size_t)n_mats * mp * k * 2;
 }
 
-size_t esp_dense_z_bytes(int m) { return (size_t)2 * device_sms() * CTAS_PER_SM * m * 128 * 4; }
+size_t esp_dense_z_bytes(int m) { return (size_t)device_sms() * CTAS_PER_SM * m * 128 * 8; }
 
 int esp_dense(const void* x, int x_dtype, long long x_stride, int m, int k, const esp_matrix_t* mats, int n_mats,
               int k2, int cb, void* y, int y_dtype, long long y_stride, void* xh, size_t xh_bytes, float* z,
@@ -894,8 +962,9 @@ namespace {
 constexpr int NOALLOC_MAX_K = 4096;            // input features
 constexpr int NOALLOC_MAX_BLOCKS = 8192;       // 128-column blocks of all matrices of one call (1,048,576 columns)
 constexpr int NOALLOC_MAX_SMS = 160;
-// partial sums: 2 slots a CTA (CTAS_PER_SM a streaming multiprocessor) x 32 rows x 128 columns
-constexpr size_t NOALLOC_Z = (size_t)2 * NOALLOC_MAX_SMS * CTAS_PER_SM * 32 * 128 * 4;
+// tagged partial sums: one slot a CTA (CTAS_PER_SM a streaming multiprocessor) x 32 rows x 128 columns x 8 bytes;
+// zero at load (static storage) and left zero by every call that completes
+constexpr size_t NOALLOC_Z = (size_t)NOALLOC_MAX_SMS * CTAS_PER_SM * 32 * 128 * 8;
 constexpr size_t NOALLOC_XH = (size_t)MAX_SHARDS * 32 * NOALLOC_MAX_K * 2;
 constexpr size_t NOALLOC_CNT = (size_t)NOALLOC_MAX_BLOCKS * 4;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_Z + NOALLOC_XH + NOALLOC_CNT];   // 6.0 MiB
@@ -950,8 +1019,5 @@ extern "C" int esp_dense_noalloc(const void* x, int x_dtype, long long x_stride,
     if (int rc = dense_plan(x, x_dtype, x_stride, m, k, mats, n_mats, k2, cb, y, y_dtype, y_stride, xh, NOALLOC_XH, z,
                             NOALLOC_Z, counters, NOALLOC_MAX_BLOCKS, pl))
         return rc;
-    // the counters must start at zero; a call that completes leaves them zero, this also covers one that did not
-    const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)pl.p.NB * 4, static_cast<cudaStream_t>(stream));
-    ESP_REQUIRE(e == cudaSuccess, ESP_ERR_CUDA, "esp_dense_noalloc: clearing counters: %s", cudaGetErrorString(e));
     return dense_run(pl, stream);
 }

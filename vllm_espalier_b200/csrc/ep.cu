@@ -2,31 +2,34 @@
 //
 // Rank q holds routed experts [q E / world, (q + 1) E / world) and the shared expert; each rank routes its own R rows.
 // Instead of two collectives a layer, the rows and the results move by stores into the other ranks' memory, mapped
-// into this process through CUDA IPC handles (no multicast objects), with release / acquire flags at system scope:
+// into this process through CUDA IPC handles (no multicast objects), with release / acquire flags at system scope.
+// A layer is four launches: routing, esp_ep_in, the expert layer kernel, esp_ep_out.
 //
-//   esp_ep_dispatch  every row to the ranks owning at least one of its routed picks and to its own rank (which
-//                    computes the shared slot) (x row: D values), every row's
-//                    pick list to every rank; then, per destination, a release store of the call's epoch into that
-//                    rank's flag word for this source
-//   esp_ep_recv      waits (bounded) for every source's flag, then writes the local pick table: a pick owned here
-//                    becomes its local expert id, the shared slot of this rank's own rows the local shared entry, every
-//                    other slot -1 (the expert kernels skip it)
-//   (grouping, rot_in and the expert kernels run on the received rows, writing y per slot)
-//   esp_ep_return    each locally computed slot's y row (D fp32) to its home rank's inbox, then a release flag per
-//                    home rank: only owned slots cross NVLink
-//   esp_ep_finish    waits (bounded) for every owner's flag, combines each row's routed slots in slot order with fp32
-//                    fused multiply-adds from 0 and writes the gated shared slot (the single-GPU layer's arithmetic on
-//                    the same y values, so outputs are bit-identical to one GPU), then advances the epoch
+//   esp_ep_in   (dispatch) CTA q < world stores every row of this rank that has a routed pick owned by rank q (all
+//               rows when q is this rank, which computes their shared slots) and every row's pick list into rank q's
+//               inboxes, then a release store of the call's epoch into q's flag word for this source;
+//               (receive) CTA 0 waits (bounded) for every source's flag, writes the local pick table (a pick owned
+//               here becomes its local expert id, the shared slot of this rank's own rows the local shared entry,
+//               every other slot -1) and its grouping (esp_group's), and publishes them;
+//               (rotate) then every CTA rotates a share of the received slots' rows for the expert kernels (rot_in)
+//   esp_ep_out  (return) CTAs (h, part) store each locally computed slot's y row (D fp32) into its home rank h's
+//               inbox, then a release flag per home rank: only owned slots cross NVLink;
+//               (finish) CTA r waits (bounded) for every owner's flag and combines row r's routed slots in slot order
+//               with fp32 fused multiply-adds from 0 and the gated shared slot (the single-GPU layer's arithmetic on
+//               the same y values, so outputs are bit-identical to one GPU); the last CTA advances the epoch
 //
-// The epoch is a device word every kernel of a call reads and the last kernel of the call increments, so a CUDA graph
-// of the step replays correctly. A rank writes another rank's inbox for call k + 1 only after its own call k has
-// finished, which waited for every owner's return of call k, which each owner issued after reading its own inbox of
-// call k: no inbox is overwritten while it is read. Waits give up after WAIT_NS, record ESP_ERR_TIMEOUT and return.
+// The epoch is a device word every kernel of a call reads and the last CTA of esp_ep_out increments once every CTA
+// of that launch has read it, so a CUDA graph of the step replays correctly. A rank writes another rank's inbox for
+// call k + 1 only after its own call k has finished, which waited for every owner's return of call k, which each
+// owner issued after reading its own inbox of call k: no inbox is overwritten while it is read. Waits give up after
+// WAIT_NS, record ESP_ERR_TIMEOUT and return.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
+#include "group.cuh"
 #include "host.hpp"
 
 ESP_DEFINE_STATUS_READER(ep)
@@ -77,137 +80,176 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 
-// CTA q: the rows of this rank that have a routed pick owned by rank q (x, D values each; all rows when q is this
-// rank, which computes their shared slots) and every row's picks.
-__global__ void __launch_bounds__(EP_THREADS) ep_dispatch_kernel(const uint16_t* __restrict__ x, long long x_stride,
-                                                                 int R, int D, const int* __restrict__ pick, int slots,
-                                                                 int n_routed, int E, int world, int rank,
-                                                                 Peers inbox_x, Peers inbox_pick, FlagPeers flags,
-                                                                 const int* __restrict__ epoch) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int q = blockIdx.x;
-    uint16_t* dx = static_cast<uint16_t*>(inbox_x.ptr[q]) + (size_t)rank * R * D;
-    int* dp = static_cast<int*>(inbox_pick.ptr[q]) + (size_t)rank * R * slots;
-    for (int i = threadIdx.x; i < R * slots; i += EP_THREADS) dp[i] = pick[i];
-    const int chunks = D / 8;                  // 16-byte pieces of a row
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = warp; r < R; r += EP_THREADS / 32) {
-        bool mine = false;
-        for (int j = 0; j < n_routed; ++j) {
-            const int e = pick[r * slots + j];
-            mine |= e >= 0 && e < E && owner_of(e, world, E) == q;
-        }
-        if (!mine && q != rank) continue;   // the home rank takes all its rows: it computes their shared slots
-        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)r * x_stride);
-        uint4* dst = reinterpret_cast<uint4*>(dx + (size_t)r * D);
-        for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        st_release_sys(flags.ptr[q] + rank, *epoch + 1);
-    }
-}
+struct InParams {
+    const uint16_t* x;                 // this rank's rows [R] (row stride x_stride), bf16 / fp16 bits
+    long long x_stride;
+    int R, D, slots, n_routed, E, world, rank;
+    const int* pick;                   // this rank's picks [R][slots], global ids (the shared slot last, id E)
+    Peers inbox_x, inbox_pick;         // every rank's inboxes: x [world][R][D], picks [world][R][slots]
+    FlagPeers flags_x;                 // every rank's flag words [world] (one a source)
+    const int* epoch;
+    const int* my_pick;                // this rank's inboxes and flags
+    const int* my_flags;
+    int* lp;                           // out: local pick table [world][R][slots]
+    int* uids; int* ucount; int* members;
+    int maxm, maxu;
+    RotIn rot;                         // suh (stacked [nl + 1][D], gate / up) and the rotated rows [world R slots][D]
+    int* counter;                      // 2 words, zero on entry and left zero
+};
 
-// One CTA: every source's flag, then the local pick table lp[s][r][j].
-__global__ void __launch_bounds__(EP_THREADS) ep_recv_kernel(const int* __restrict__ inbox_pick, const int* flags,
-                                                             const int* __restrict__ epoch, int world, int rank, int R,
-                                                             int slots, int n_routed, int E, int* __restrict__ lp) {
-    pdl_launch_dependents();
-    pdl_wait();
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        const int need = *epoch + 1;
-        bool ok = true;
-        for (int s = 0; s < world && ok; ++s) ok = wait_flag_sys(flags + s, need);
-        s_ok = ok;
-    }
-    __syncthreads();
-    const int e0 = rank * E / world, e1 = (rank + 1) * E / world, nl = e1 - e0;
-    const int n = world * R * slots;
-    for (int i = threadIdx.x; i < n; i += EP_THREADS) {
-        int v = -1;
-        if (s_ok) {
-            const int e = inbox_pick[i];
-            const int j = i % slots, s = i / (R * slots);
-            if (j < n_routed) v = (e >= e0 && e < e1) ? e - e0 : -1;
-            else v = (s == rank && e >= 0) ? nl : -1;   // the shared slot: computed on the row's home rank only
-        }
-        lp[i] = v;
-    }
-}
-
-// CTA h (grid x = world): this rank's y rows of the slots whose home is rank h, into h's inbox [R][slots][D], then a
-// release flag in h's flag word for this owner. Other CTAs along y share the copying of one home's rows.
-__global__ void __launch_bounds__(EP_THREADS) ep_return_kernel(const float* __restrict__ y, const int* __restrict__ lp,
-                                                               int R, int slots, int D, int rank, Peers inbox_y,
-                                                               FlagPeers flags, const int* __restrict__ epoch,
-                                                               int* __restrict__ done) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int h = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wpc = EP_THREADS / 32, nw = wpc * gridDim.y;
-    float* dst = static_cast<float*>(inbox_y.ptr[h]);
-    const int base = h * R * slots;
-    for (int i = blockIdx.y * wpc + warp; i < R * slots; i += nw) {
-        if (lp[base + i] < 0) continue;
-        const float4* src = reinterpret_cast<const float4*>(y + (size_t)(base + i) * D);
-        float4* d = reinterpret_cast<float4*>(dst + (size_t)i * D);
-        for (int c = lane; c < D / 4; c += 32) d[c] = src[c];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();   // this CTA's stores before the arrival that may release the flag
-        if (atomicAdd(done + h, 1) == (int)gridDim.y - 1) {
-            __threadfence_system();
-            done[h] = 0;
-            st_release_sys(flags.ptr[h] + rank, *epoch + 1);
-        }
-    }
-}
-
-// One CTA a row: every owner's flag, then out[r] = slot-ordered fp32 fma of the routed slots' y from 0, and
-// out_shared[r] = w_shared * y_shared (esp_ep_combine's arithmetic); the last CTA advances the epoch.
+// Dispatch, receive, group and rotate in one launch (see the top of the file). x of dtype T.
 template <typename T>
-__global__ void __launch_bounds__(EP_THREADS) ep_finish_kernel(const float* __restrict__ inbox_y, const int* flags,
-                                                               const int* __restrict__ pick, const float* __restrict__ wts,
-                                                               T* __restrict__ out, T* __restrict__ out_shared, int R,
-                                                               int D, int slots, int n_routed, int E, int world,
-                                                               int* epoch, int* count) {
+__global__ void __launch_bounds__(EP_THREADS) ep_in_kernel(const __grid_constant__ InParams p) {
+    __shared__ int sh_lp[MAX_PICKS];
+    __shared__ int s_ok;
     pdl_launch_dependents();
     pdl_wait();
-    __shared__ int s_ok;
-    const int r = blockIdx.x;
-    if (threadIdx.x == 0) {
-        const int need = *epoch + 1;
-        bool ok = true;
-        for (int s = 0; s < world && ok; ++s) ok = wait_flag_sys(flags + s, need);
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (s_ok) {
-        for (int n = threadIdx.x; n < D; n += EP_THREADS) {
-            float acc = 0.f;
-            for (int j = 0; j < n_routed; ++j) {
-                const int e = pick[r * slots + j];
-                if (e < 0 || e >= E) continue;
-                acc = __fmaf_rn(wts[r * slots + j], inbox_y[((size_t)r * slots + j) * D + n], acc);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = p.R, D = p.D, slots = p.slots;
+    if ((int)blockIdx.x < p.world) {   // ---- dispatch to rank q ----
+        const int q = blockIdx.x;
+        uint16_t* dx = static_cast<uint16_t*>(p.inbox_x.ptr[q]) + (size_t)p.rank * R * D;
+        int* dp = static_cast<int*>(p.inbox_pick.ptr[q]) + (size_t)p.rank * R * slots;
+        for (int i = threadIdx.x; i < R * slots; i += EP_THREADS) dp[i] = p.pick[i];
+        for (int r = warp; r < R; r += EP_THREADS / 32) {
+            bool mine = false;
+            for (int j = 0; j < p.n_routed; ++j) {
+                const int e = p.pick[r * slots + j];
+                mine |= e >= 0 && e < p.E && owner_of(e, p.world, p.E) == q;
             }
-            out[(size_t)r * D + n] = from_f32<T>(acc);
-            if (out_shared && slots > n_routed) {
-                const int j = n_routed;
-                const float v = pick[r * slots + j] >= 0 ? wts[r * slots + j] * inbox_y[((size_t)r * slots + j) * D + n]
-                                                         : 0.f;
-                out_shared[(size_t)r * D + n] = from_f32<T>(v);
+            if (!mine && q != p.rank) continue;   // the home rank takes all its rows: it computes their shared slots
+            const uint4* src = reinterpret_cast<const uint4*>(p.x + (size_t)r * p.x_stride);
+            uint4* dst = reinterpret_cast<uint4*>(dx + (size_t)r * D);
+            for (int c = lane; c < D / 8; c += 32) dst[c] = src[c];
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            st_release_sys(p.flags_x.ptr[q] + p.rank, *p.epoch + 1);
+        }
+    }
+    const int e0 = p.rank * p.E / p.world, e1 = (p.rank + 1) * p.E / p.world, nl = e1 - e0;
+    const int n = p.world * R * slots;
+    if (blockIdx.x == 0) {             // ---- receive: every source's flag, the local table and its grouping ----
+        if (threadIdx.x == 0) {
+            const int need = *p.epoch + 1;
+            bool ok = true;
+            for (int s = 0; s < p.world && ok; ++s) ok = wait_flag_sys(p.my_flags + s, need);
+            s_ok = ok;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += EP_THREADS) {
+            int v = -1;
+            if (s_ok) {
+                const int e = __ldcv(p.my_pick + i);
+                const int j = i % slots, src = i / (R * slots);
+                if (j < p.n_routed) v = (e >= e0 && e < e1) ? e - e0 : -1;
+                else v = (src == p.rank && e >= 0) ? nl : -1;   // the shared slot: computed on the row's home rank
+            }
+            sh_lp[i] = v;
+            p.lp[i] = v;
+        }
+        __syncthreads();
+        group_block(sh_lp, n, slots, nl + 1, p.uids, p.ucount, p.members, p.maxm, p.maxu);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            st_release_gpu(p.counter, 1);
+        }
+    }
+    // ---- rotate: every CTA, once the table is published ----
+    __shared__ int s_go;
+    if (threadIdx.x == 0) s_go = wait_flag_gpu(p.counter, 1);
+    __syncthreads();
+    if (s_go) rotate_share<T>(reinterpret_cast<const T*>(p.inbox_x.ptr[p.rank]), D, D, p.lp, n, slots, p.rot);
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(p.counter + 1, 1) == (int)gridDim.x - 1) {   // every CTA is past its wait
+        p.counter[0] = 0;
+        p.counter[1] = 0;
+    }
+}
+
+struct OutParams {
+    const float* y;                    // this rank's expert output [world][R][slots][D] fp32
+    const int* lp;                     // the local pick table of the call
+    int R, D, slots, n_routed, E, world, rank, split;
+    Peers inbox_y;                     // every rank's inbox [R][slots][D] fp32
+    FlagPeers flags_y;
+    const int* my_flags;
+    const float* my_y;                 // this rank's inbox
+    const int* pick;                   // this rank's picks [R][slots] (global ids) and weights
+    const float* wts;
+    void* out; void* out_shared;       // [R][D] of dtype T
+    int* epoch;
+    int* done;                         // [world], zero on entry and left zero
+    int* count;                        // zero on entry and left zero
+};
+
+// Return and finish in one launch (see the top of the file): CTAs [0, world * split) return, CTA world * split + r
+// finishes row r. Every CTA is resident (at most 8 * 4 + 32), so the finishing CTAs' waits on this rank's own
+// returns end.
+template <typename T>
+__global__ void __launch_bounds__(EP_THREADS) ep_out_kernel(const __grid_constant__ OutParams p) {
+    __shared__ int s_ok;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = p.R, D = p.D, slots = p.slots;
+    const int need = *p.epoch + 1;
+    const int nret = p.world * p.split;
+    if ((int)blockIdx.x < nret) {      // ---- return: this rank's y rows of home h's slots ----
+        const int h = blockIdx.x / p.split, part = blockIdx.x % p.split;
+        const int wpc = EP_THREADS / 32, nw = wpc * p.split;
+        float* dst = static_cast<float*>(p.inbox_y.ptr[h]);
+        const int base = h * R * slots;
+        for (int i = part * wpc + warp; i < R * slots; i += nw) {
+            if (__ldcg(p.lp + base + i) < 0) continue;
+            const float4* src = reinterpret_cast<const float4*>(p.y + (size_t)(base + i) * D);
+            float4* d = reinterpret_cast<float4*>(dst + (size_t)i * D);
+            for (int c = lane; c < D / 4; c += 32) d[c] = __ldcg(src + c);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();   // this CTA's stores before the arrival that may release the flag
+            if (atomicAdd(p.done + h, 1) == p.split - 1) {
+                __threadfence_system();
+                p.done[h] = 0;
+                st_release_sys(p.flags_y.ptr[h] + p.rank, need);
+            }
+        }
+    } else {                           // ---- finish row r ----
+        const int r = blockIdx.x - nret;
+        if (threadIdx.x == 0) {
+            bool ok = true;
+            for (int s = 0; s < p.world && ok; ++s) ok = wait_flag_sys(p.my_flags + s, need);
+            s_ok = ok;
+        }
+        __syncthreads();
+        if (s_ok) {
+            T* out = static_cast<T*>(p.out);
+            T* out_shared = static_cast<T*>(p.out_shared);
+            for (int c = threadIdx.x; c < D; c += EP_THREADS) {
+                float acc = 0.f;
+                for (int j = 0; j < p.n_routed; ++j) {
+                    const int e = p.pick[r * slots + j];
+                    if (e < 0 || e >= p.E) continue;
+                    acc = __fmaf_rn(p.wts[r * slots + j], __ldcv(p.my_y + ((size_t)r * slots + j) * D + c), acc);
+                }
+                out[(size_t)r * D + c] = from_f32<T>(acc);
+                if (out_shared && slots > p.n_routed) {
+                    const int j = p.n_routed;
+                    const float v = p.pick[r * slots + j] >= 0
+                                        ? p.wts[r * slots + j] * __ldcv(p.my_y + ((size_t)r * slots + j) * D + c)
+                                        : 0.f;
+                    out_shared[(size_t)r * D + c] = from_f32<T>(v);
+                }
             }
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(count, 1) == (int)gridDim.x - 1) {
-        *count = 0;
-        *epoch += 1;
+    if (threadIdx.x == 0 && atomicAdd(p.count, 1) == (int)gridDim.x - 1) {   // every CTA has read the epoch
+        *p.count = 0;
+        *p.epoch += 1;
     }
 }
 
@@ -256,85 +298,82 @@ int esp_ipc_free(void* ptr) {
     return ok();
 }
 
-int esp_ep_dispatch(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots,
-                    int n_routed, int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick,
-                    int* const* flags_x, const int* epoch, void* stream) {
-    ESP_REQUIRE(x && pick && inbox_x && inbox_pick && flags_x && epoch, ESP_ERR_INVALID, "ep_dispatch: null pointer");
+int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots, int n_routed,
+              int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick, int* const* flags_x,
+              const int* epoch, int* local_pick, int* uids, int* ucount, int* members, int maxm, int maxu,
+              const void* suh_gate, const void* suh_up, void* xg, void* xu, int* counter, void* stream) {
+    ESP_REQUIRE(x && pick && inbox_x && inbox_pick && flags_x && epoch && local_pick && uids && ucount && members &&
+                    suh_gate && suh_up && xg && xu && counter,
+                ESP_ERR_INVALID, "ep_in: null pointer");
     ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world, ESP_ERR_INVALID,
-                "ep_dispatch: 1 to %d ranks", EP_MAX_WORLD);
-    ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "ep_dispatch: bf16/fp16 rows");
-    ESP_REQUIRE(R >= 1 && R <= 32 && D % 8 == 0 && x_stride >= D && x_stride % 8 == 0 && aligned(x, 16),
-                ESP_ERR_INVALID, "ep_dispatch: 1..32 rows of 16-byte aligned D values");
-    ESP_REQUIRE(slots >= 1 && slots <= 32 && n_routed <= slots && E >= world, ESP_ERR_INVALID, "ep_dispatch: slots");
-    Peers px = {}, pp = {};
-    FlagPeers pf = {};
+                "ep_in: 1 to %d ranks", EP_MAX_WORLD);
+    ESP_REQUIRE(x_dtype == ESP_DTYPE_BF16 || x_dtype == ESP_DTYPE_F16, ESP_ERR_INVALID, "ep_in: bf16/fp16 rows");
+    ESP_REQUIRE(R >= 1 && R <= 32 && D % 128 == 0 && x_stride >= D && x_stride % 8 == 0 && aligned(x, 16),
+                ESP_ERR_INVALID, "ep_in: 1..32 rows of 16-byte aligned D values (D a multiple of 128)");
+    ESP_REQUIRE(slots >= 1 && slots <= 32 && n_routed <= slots && E >= world && world * R * slots <= MAX_PICKS,
+                ESP_ERR_INVALID, "ep_in: slots");
+    const int nl = (rank + 1) * E / world - rank * E / world;
+    ESP_REQUIRE(nl + 1 <= MAX_E && maxm >= 1 && maxm <= 32 && maxu >= 1, ESP_ERR_INVALID, "ep_in: grouping limits");
+    InParams p{};
+    p.x = static_cast<const uint16_t*>(x);
+    p.x_stride = x_stride;
+    p.R = R; p.D = D; p.slots = slots; p.n_routed = n_routed; p.E = E; p.world = world; p.rank = rank;
+    p.pick = pick;
     for (int q = 0; q < world; ++q) {
-        ESP_REQUIRE(inbox_x[q] && inbox_pick[q] && flags_x[q], ESP_ERR_INVALID, "ep_dispatch: rank %d's buffers", q);
-        px.ptr[q] = inbox_x[q];
-        pp.ptr[q] = inbox_pick[q];
-        pf.ptr[q] = flags_x[q];
+        ESP_REQUIRE(inbox_x[q] && inbox_pick[q] && flags_x[q], ESP_ERR_INVALID, "ep_in: rank %d's buffers", q);
+        p.inbox_x.ptr[q] = inbox_x[q];
+        p.inbox_pick.ptr[q] = inbox_pick[q];
+        p.flags_x.ptr[q] = flags_x[q];
     }
-    if (int rc = launch(ep_dispatch_kernel, dim3(world), dim3(EP_THREADS), 0, stream, true,
-                        static_cast<const uint16_t*>(x), x_stride, R, D, pick, slots, n_routed, E, world, rank, px, pp,
-                        pf, epoch))
-        return rc;
+    p.epoch = epoch;
+    p.my_pick = static_cast<const int*>(inbox_pick[rank]);
+    p.my_flags = flags_x[rank];
+    p.lp = local_pick;
+    p.uids = uids; p.ucount = ucount; p.members = members; p.maxm = maxm; p.maxu = maxu;
+    p.rot.suh[0] = static_cast<const __half*>(suh_gate);
+    p.rot.suh[1] = static_cast<const __half*>(suh_up);
+    p.rot.out[0] = static_cast<__half*>(xg);
+    p.rot.out[1] = static_cast<__half*>(xu);
+    p.rot.E_tab = nl + 1;
+    p.counter = counter;
+    // about four rotation tasks (a matrix, a slot, a 128-block) a warp, at least a CTA a destination, one wave
+    const int tasks = 2 * world * R * slots * (D / 128);
+    const int grid = std::max(world, std::min(device_sms(), (tasks + 4 * (EP_THREADS / 32) - 1) / (4 * (EP_THREADS / 32))));
+    int rc = x_dtype == ESP_DTYPE_BF16
+                 ? launch(ep_in_kernel<__nv_bfloat16>, dim3(grid), dim3(EP_THREADS), 0, stream, true, p)
+                 : launch(ep_in_kernel<__half>, dim3(grid), dim3(EP_THREADS), 0, stream, true, p);
+    if (rc) return rc;
     return ok();
 }
 
-int esp_ep_recv(const int* inbox_pick, const int* flags_x, const int* epoch, int world, int rank, int R, int slots,
-                int n_routed, int E, int* local_pick, void* stream) {
-    ESP_REQUIRE(inbox_pick && flags_x && epoch && local_pick, ESP_ERR_INVALID, "ep_recv: null pointer");
+int esp_ep_out(const float* y, const int* local_pick, int world, int rank, int R, int slots, int n_routed, int E,
+               int D, float* const* inbox_y, int* const* flags_y, const int* pick, const float* wts, void* out,
+               void* out_shared, int out_dtype, int* epoch, int* done, int* count, void* stream) {
+    ESP_REQUIRE(y && local_pick && inbox_y && flags_y && pick && wts && out && epoch && done && count, ESP_ERR_INVALID,
+                "ep_out: null pointer");
     ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world && R >= 1 && R <= 32 &&
-                    slots >= 1 && slots <= 32 && n_routed <= slots && E >= world,
-                ESP_ERR_INVALID, "ep_recv: limits");
-    if (int rc = launch(ep_recv_kernel, dim3(1), dim3(EP_THREADS), 0, stream, true, inbox_pick, flags_x, epoch, world,
-                        rank, R, slots, n_routed, E, local_pick))
-        return rc;
-    return ok();
-}
-
-int esp_ep_return(const float* y, const int* local_pick, int world, int rank, int R, int slots, int D,
-                  float* const* inbox_y, int* const* flags_y, const int* epoch, int* done, void* stream) {
-    ESP_REQUIRE(y && local_pick && inbox_y && flags_y && epoch && done, ESP_ERR_INVALID, "ep_return: null pointer");
-    ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world && R >= 1 && R <= 32 &&
-                    slots >= 1 && slots <= 32 && D % 4 == 0,
-                ESP_ERR_INVALID, "ep_return: limits");
-    Peers py = {};
-    FlagPeers pf = {};
-    for (int q = 0; q < world; ++q) {
-        ESP_REQUIRE(inbox_y[q] && flags_y[q], ESP_ERR_INVALID, "ep_return: rank %d's buffers", q);
-        py.ptr[q] = inbox_y[q];
-        pf.ptr[q] = flags_y[q];
-    }
-    const int split = R * slots > 64 ? 4 : 1;
-    if (int rc = launch(ep_return_kernel, dim3(world, split), dim3(EP_THREADS), 0, stream, true, y, local_pick, R,
-                        slots, D, rank, py, pf, epoch, done))
-        return rc;
-    return ok();
-}
-
-int esp_ep_finish(const float* inbox_y, const int* flags_y, const int* pick, const float* wts, void* out,
-                  void* out_shared, int out_dtype, int R, int D, int slots, int n_routed, int E, int world, int* epoch,
-                  int* count, void* stream) {
-    ESP_REQUIRE(inbox_y && flags_y && pick && wts && out && epoch && count, ESP_ERR_INVALID, "ep_finish: null pointer");
-    ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && R >= 1 && R <= 32 && slots >= 1 && slots <= 32 &&
-                    n_routed <= slots && E >= world,
-                ESP_ERR_INVALID, "ep_finish: limits");
+                    slots >= 1 && slots <= 32 && n_routed <= slots && E >= world && D % 4 == 0,
+                ESP_ERR_INVALID, "ep_out: limits");
     ESP_REQUIRE(out_dtype == ESP_DTYPE_BF16 || out_dtype == ESP_DTYPE_F16 || out_dtype == ESP_DTYPE_F32, ESP_ERR_INVALID,
-                "ep_finish: dtype");
+                "ep_out: dtype");
+    OutParams p{};
+    p.y = y; p.lp = local_pick;
+    p.R = R; p.D = D; p.slots = slots; p.n_routed = n_routed; p.E = E; p.world = world; p.rank = rank;
+    p.split = R * slots > 64 ? 4 : 1;
+    for (int q = 0; q < world; ++q) {
+        ESP_REQUIRE(inbox_y[q] && flags_y[q], ESP_ERR_INVALID, "ep_out: rank %d's buffers", q);
+        p.inbox_y.ptr[q] = inbox_y[q];
+        p.flags_y.ptr[q] = flags_y[q];
+    }
+    p.my_flags = flags_y[rank];
+    p.my_y = inbox_y[rank];
+    p.pick = pick; p.wts = wts; p.out = out; p.out_shared = out_shared;
+    p.epoch = epoch; p.done = done; p.count = count;
+    const dim3 grid(world * p.split + R);
     int rc;
-    if (out_dtype == ESP_DTYPE_BF16)
-        rc = launch(ep_finish_kernel<__nv_bfloat16>, dim3(R), dim3(EP_THREADS), 0, stream, true, inbox_y, flags_y, pick,
-                    wts, static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(out_shared), R, D, slots,
-                    n_routed, E, world, epoch, count);
-    else if (out_dtype == ESP_DTYPE_F16)
-        rc = launch(ep_finish_kernel<__half>, dim3(R), dim3(EP_THREADS), 0, stream, true, inbox_y, flags_y, pick, wts,
-                    static_cast<__half*>(out), static_cast<__half*>(out_shared), R, D, slots, n_routed, E, world, epoch,
-                    count);
-    else
-        rc = launch(ep_finish_kernel<float>, dim3(R), dim3(EP_THREADS), 0, stream, true, inbox_y, flags_y, pick, wts,
-                    static_cast<float*>(out), static_cast<float*>(out_shared), R, D, slots, n_routed, E, world, epoch,
-                    count);
+    if (out_dtype == ESP_DTYPE_BF16) rc = launch(ep_out_kernel<__nv_bfloat16>, grid, dim3(EP_THREADS), 0, stream, true, p);
+    else if (out_dtype == ESP_DTYPE_F16) rc = launch(ep_out_kernel<__half>, grid, dim3(EP_THREADS), 0, stream, true, p);
+    else rc = launch(ep_out_kernel<float>, grid, dim3(EP_THREADS), 0, stream, true, p);
     if (rc) return rc;
     return ok();
 }

@@ -27,7 +27,8 @@ MAX_PER_LAUNCH = 4
 
 
 class Workspace:
-    """The dense kernel's scratch on one device: xh fp16, z fp32, counters int32 (zero on entry, left zero)."""
+    """The dense kernel's scratch on one device: xh fp16, z (tagged partial sums, 8-byte words, zero on entry and left
+    zero), counters int32 (zero)."""
 
     def __init__(self, device: torch.device):
         self.device = device
@@ -39,7 +40,7 @@ class Workspace:
         if self.xh.numel() * 2 < xh_bytes:
             self.xh = self._new(-(-xh_bytes // 2), torch.float16, zero=False)
         if self.z.numel() * 4 < z_bytes:
-            self.z = self._new(-(-z_bytes // 4), torch.float32, zero=False)
+            self.z = self._new(-(-z_bytes // 4), torch.float32, zero=True)
         if self.counters.numel() < blocks:
             self.counters = self._new(blocks, torch.int32, zero=True)
         return self

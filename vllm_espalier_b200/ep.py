@@ -18,10 +18,11 @@ layer, with outputs bit-identical to it for every world size:
 
 The exchange (ESPALIER_EP_EXCHANGE): `p2p` (default) moves rows and results by stores into the other ranks' memory
 (csrc/ep.cu, PeerExchange below): a row goes only to the ranks owning one of its picks, a slot's y row only from its
-owner to its home rank, with release / acquire flags instead of collectives, 4 small launches around the expert
-kernels and nothing on the host; `nccl` is the two-collective form above. The index logic of the `nccl` form (local
+owner to its home rank, with release / acquire flags instead of collectives; a layer is four launches (routing,
+esp_ep_in = dispatch + receive + grouping + rotation, the one-launch expert kernel, esp_ep_out = return + combine)
+and nothing on the host; `nccl` is the two-collective form above. The index logic of the `nccl` form (local
 tables, owners, buffer layouts) is in plain torch functions shared with the CPU tests (gloo ranks with a stand-in
-expert function); the `p2p` form computes the same table on the device (esp_ep_recv).
+expert function); the `p2p` form computes the same table on the device (esp_ep_in).
 """
 from __future__ import annotations
 
@@ -170,14 +171,17 @@ class EPLayer:
         self.xg = torch.zeros((P, D), dtype=torch.float16, device=dev)
         self.xu = torch.zeros((P, D), dtype=torch.float16, device=dev)
         self.xd = torch.zeros((P, I), dtype=torch.float16, device=dev)
-        self.z = torch.zeros((2 * self.S * P * I,), dtype=torch.float32, device=dev)
+        self.z = torch.zeros((P * max(2 * self.S * I, D),), dtype=torch.float32, device=dev)
         self.y = torch.zeros((P, D), dtype=torch.float32, device=dev)
         self.ids = torch.zeros((self.maxu,), dtype=torch.int32, device=dev)
         self.count = torch.zeros((1,), dtype=torch.int32, device=dev)
         self.members = torch.full((self.maxu, MAXM), -1, dtype=torch.int32, device=dev)
         self.cnt_gu = torch.zeros((self.maxu * (I // 128) + 1,), dtype=torch.int32, device=dev)
         self.cnt_d = torch.zeros((world * rows * (D // 128) + 1,), dtype=torch.int32, device=dev)
+        self.cnt_layer = torch.zeros((int(lib().esp_moe_layer_counters(self.maxu, world * rows, D, I)),),
+                                     dtype=torch.int32, device=dev)
         self.no_w = torch.zeros((P,), dtype=torch.float32, device=dev)
+        self.in_counter = torch.zeros((2,), dtype=torch.int32, device=dev)   # esp_ep_in's publication words
         self.no_out = torch.empty((world * rows, D), dtype=torch.bfloat16, device=dev)
         self.exchange = EP_EXCHANGE
         self.ex = None          # the PeerExchange, made at the first p2p forward (it needs the rows' dtype)
@@ -201,16 +205,23 @@ class EPLayer:
         return self.y[:world * R * self.slots].view(world, R, self.slots, D)
 
     def _run_experts(self, rows_x, stride: int, rows: int, lpf: torch.Tensor):
-        e = ext()
-        D, slots = self.L.D, self.slots
-        P = rows * slots
-        L = self.L
+        e, L, D, slots = ext(), self.L, self.L.D, self.slots
         e.group(lpf, self.ids, self.count, self.members, rows, slots, self.nl + 1)
         e.rot_in(rows_x, stride, lpf, L.gate.suh, L.up.suh, self.xg, self.xu, rows, D, slots, self.nl + 1)
-        e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, P, self.S, self.z, self.cnt_gu,
-                     self.xd)
-        e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
-                   self.cnt_d, self.no_out[:rows], None)
+        self._expert_kernels(rows, lpf)
+
+    def _expert_kernels(self, rows: int, lpf: torch.Tensor):
+        """The y rows of every slot with a local pick (xg / xu rotated, the grouping in ids / count / members); no
+        combine here (n_routed 0: the home rank combines)."""
+        e, L, slots = ext(), self.L, self.slots
+        if X.MOE_ONE_LAUNCH:
+            e.moe_layer(self.xg, self.xu, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.S,
+                        self.z, self.xd, self.y, self.cnt_layer, self.no_out[:rows], None)
+        else:
+            e.moe_gateup(self.xg, self.xu, L, self.ids, self.count, self.members, slots, rows * slots, self.S, self.z,
+                         self.cnt_gu, self.xd)
+            e.moe_down(self.xd, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.y,
+                       self.cnt_d, self.no_out[:rows], None)
 
     def forward(self, x: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
                 out_shared: torch.Tensor | None = None, group=None):
@@ -232,7 +243,8 @@ class EPLayer:
         return out, out_shared
 
     def _forward_p2p(self, x, gate, out, out_shared, group):
-        """The same layer with the peer-store exchange: route, dispatch, receive, experts, return, finish."""
+        """The same layer with the peer-store exchange, four launches: routing; esp_ep_in (dispatch, receive, grouping,
+        the experts' input rotation); the expert layer kernel; esp_ep_out (return, finish)."""
         R, D = x.shape
         if R > self.rows:
             raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
@@ -242,17 +254,16 @@ class EPLayer:
         world, rank, slots, k = self.world, self.rank, self.slots, self.k
         pick, wts = self.route(x, gate)
         x = x if x.stride(1) == 1 else x.contiguous()
-        check(h.esp_ep_dispatch(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, D, pick.data_ptr(), slots, k, self.E,
-                                world, rank, ex.peer["x"], ex.peer["pick"], ex.peer["flags_x"], ex.local("epoch"), st))
-        lp = ex.lp[:world * R * slots]
-        check(h.esp_ep_recv(ex.local("pick"), ex.local("flags_x"), ex.local("epoch"), world, rank, R, slots, k, self.E,
-                            lp.data_ptr(), st))
-        self._run_experts(ex.inbox_x, D, world * R, lp)
-        check(h.esp_ep_return(self.y.data_ptr(), lp.data_ptr(), world, rank, R, slots, D, ex.peer["y"],
-                              ex.peer["flags_y"], ex.local("epoch"), ex.local("done"), st))
+        L, lp = self.L, ex.lp[:world * R * slots]
+        check(h.esp_ep_in(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, D, pick.data_ptr(), slots, k, self.E, world,
+                          rank, ex.peer["x"], ex.peer["pick"], ex.peer["flags_x"], ex.local("epoch"), lp.data_ptr(),
+                          self.ids.data_ptr(), self.count.data_ptr(), self.members.data_ptr(), MAXM, self.maxu,
+                          L.gate.suh.data_ptr(), L.up.suh.data_ptr(), self.xg.data_ptr(), self.xu.data_ptr(),
+                          self.in_counter.data_ptr(), st))
+        self._expert_kernels(world * R, lp)
         out = out if out is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
         out_shared = out_shared if out_shared is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
-        check(h.esp_ep_finish(ex.local("y"), ex.local("flags_y"), pick.data_ptr(), wts.data_ptr(), out.data_ptr(),
-                              out_shared.data_ptr(), DTYPE[out.dtype], R, D, slots, k, self.E, world, ex.local("epoch"),
-                              ex.local("count"), st))
+        check(h.esp_ep_out(self.y.data_ptr(), lp.data_ptr(), world, rank, R, slots, k, self.E, D, ex.peer["y"],
+                           ex.peer["flags_y"], pick.data_ptr(), wts.data_ptr(), out.data_ptr(), out_shared.data_ptr(),
+                           DTYPE[out.dtype], ex.local("epoch"), ex.local("done"), ex.local("count"), st))
         return out, out_shared
