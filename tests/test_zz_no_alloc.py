@@ -44,7 +44,7 @@ def _call_dense(lib, arr, n, x, N, k2, cb, dev):
     M, K = x.shape
     y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     xh = torch.empty(lib.esp_dense_xh_bytes(M, K, n) // 2, dtype=torch.float16, device=dev)
-    z = torch.empty(lib.esp_dense_z_bytes(M) // 4 + 1, dtype=torch.float32, device=dev)
+    z = torch.zeros(lib.esp_dense_z_bytes(M) // 4 + 1, dtype=torch.float32, device=dev)   # zero on entry
     cnt = torch.zeros(N // 128, dtype=torch.int32, device=dev)
     rc = lib.esp_dense(x.data_ptr(), 1, x.stride(0), M, K, arr, n, k2, cb, y.data_ptr(), 1, y.stride(0),
                        xh.data_ptr(), xh.numel() * 2, z.data_ptr(), z.numel() * 4, cnt.data_ptr(), cnt.numel(),

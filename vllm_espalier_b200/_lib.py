@@ -116,15 +116,14 @@ _private_z: dict = {}
 
 
 def _z_for(Z: torch.Tensor, M: int, device) -> torch.Tensor:
-    """The caller's Z when it holds esp_dense_z_bytes(M), else a private per-device buffer grown to that size: callers
-    that size Z by the reference's own plan (SK * 32 * N floats, vllm_espalier/dense.py:80-84) can fall short of this
-    library's split for some shapes (few k-tiles). Only the Python shim allocates; the C ABI never does."""
-    need = int(lib().esp_dense_z_bytes(M))
-    if Z.numel() * 4 >= need:
-        return Z
+    """The split-K scratch for ext().dense: a private per-device buffer, zeroed when it is made and left zero by every
+    call (the kernel's tagged partials need a zero Z on entry), sized for 32 rows. The caller's Z is accepted and not
+    used: the reference allocates it with torch.empty (vllm_espalier/dense.py:42-48), and sizes it by its own plan.
+    Only the Python shim allocates; the C ABI never does."""
+    need = int(lib().esp_dense_z_bytes(max(M, 32)))
     z = _private_z.get(device)
     if z is None or z.numel() * 4 < need:
-        z = torch.empty(need // 4, dtype=torch.float32, device=device)
+        z = torch.zeros(need // 4, dtype=torch.float32, device=device)
         _private_z[device] = z
     return z
 

@@ -22,8 +22,10 @@
 //     the last segment); every other CTA of the block holds it as its first segment and stores that partial, as
 //     tagged 64-bit words (value | 1 << 32), in its one slot of Z. The finisher reads the slots in CTA (= k) order,
 //     polling each word's tag (bounded), adds them after its own sums, and clears the slots to zero for the next
-//     launch: no fence, no atomic, and the other CTAs leave as soon as their stores are issued. A block inside one
-//     CTA's range is finished in place. Finishing = FWHT-128 of the sums, * step, * H/sqrt(128) * svh, in the
+//     launch: no fence, no atomic, and the other CTAs leave as soon as their stores are issued. With equal k-slices
+//     (S CTAs a block, the default below SMs blocks) and more than 8 rows the S CTAs share the finishing instead:
+//     slice j stores the rows it does not finish and finishes the rows r = j (mod S). The sums are the same either
+//     way (k order from 0). A block inside one CTA's range is finished in place. Finishing = FWHT-128 of the sums, * step, * H/sqrt(128) * svh, in the
 //     reference's order, then the store in y's dtype. The ranges depend on the shape and the SM count only.
 //   * Decode ahead (fused path): the weights do not depend on the previous kernel, so a CTA decodes its units into
 //     shared memory before the launch wait while the previous launch drains; when every unit of every CTA fits, all
@@ -104,6 +106,7 @@ struct DenseParams {
     float scale;                 // codebook step of the kernel form
     int npre;                    // fused path: units decoded ahead of the launch wait (whole stages, one segment)
     int ahead_all;               // fused path: every CTA decodes all of its units ahead of the wait (npre = max)
+    int kslices;                 // > 1: G = blocks * kslices equal k-slices (CTA c = block c / S, slice c % S)
     int stages;                  // ring depth in stages (<= STAGES)
 };
 
@@ -192,6 +195,60 @@ __device__ __forceinline__ float4 poll_tagged4(const uint64_t* w) {
             report(ESP_ERR_TIMEOUT);
             return make_float4(0.f, 0.f, 0.f, 0.f);
         }
+    }
+}
+
+// Row r of a block split over the n CTAs c0..c0 + n - 1 (k order), finished by CTA c0 + own: the n partials added in
+// k order from 0 (this CTA's own from red, the others' tagged Z slots, four reads in flight, a word whose tag is not
+// set yet polled, bounded), each slot row read cleared for the next launch; then the block's finishing and store.
+__device__ __forceinline__ void finish_row(const DenseParams& p, const float* red, int c0, int n, int own, int r,
+                                           const DShard& S, int bl, uint2 sv, int lane) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q4 = 0; q4 < n; q4 += 4) {
+        float4 f[4];
+        uint32_t ok = 0;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            const int q = q4 + d;
+            if (q < n && q != own) {
+                const uint64_t* w = p.Z + ((size_t)(c0 + q) * p.M + r) * 128 + 4 * lane;
+                uint64_t a, b, cc, dd;
+                ld_relaxed_v2_u64(w, a, b);
+                ld_relaxed_v2_u64(w + 2, cc, dd);
+                f[d] = make_float4(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b),
+                                   __uint_as_float((uint32_t)cc), __uint_as_float((uint32_t)dd));
+                ok |= (((a & b & cc & dd) >> 32) != 0 ? 1u : 0u) << d;
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            const int q = q4 + d;
+            if (q >= n) break;
+            if (q == own) {
+                f[d] = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+            } else {
+                uint64_t* w = p.Z + ((size_t)(c0 + q) * p.M + r) * 128 + 4 * lane;
+                if (!((ok >> d) & 1u)) f[d] = poll_tagged4(w);
+                st_relaxed_v2_u64(w, 0ull, 0ull);       // the slot row is empty again
+                st_relaxed_v2_u64(w + 2, 0ull, 0ull);
+            }
+            v[0] += f[d].x; v[1] += f[d].y; v[2] += f[d].z; v[3] += f[d].w;
+        }
+    }
+    finish_store(v, lane, S, bl, r, p, sv);
+}
+
+// This CTA's partial rows (red) in its Z slot as tagged words, the rows r with skip(r) false.
+template <typename Skip>
+__device__ __forceinline__ void store_partial(const DenseParams& p, const float* red, int c, int warp, int lane,
+                                              Skip skip) {
+    uint64_t* zs = p.Z + (size_t)c * p.M * 128;
+    for (int r = warp; r < p.M; r += CWARPS) {
+        if (skip(r)) continue;
+        const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
+        uint64_t* w = zs + r * 128 + 4 * lane;
+        st_relaxed_v2_u64(w, TAG | __float_as_uint(q.x), TAG | __float_as_uint(q.y));
+        st_relaxed_v2_u64(w + 2, TAG | __float_as_uint(q.z), TAG | __float_as_uint(q.w));
     }
 }
 
@@ -409,10 +466,6 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                 }
                 if (GROUPS > 1 && gi + 1 < GROUPS) named_sync(1, CT);
             }
-    #pragma unroll
-            for (int e = 0; e < 2; ++e)
-    #pragma unroll
-                for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
             named_sync(1, CT);
 
             const DShard& S = p.s[shard_of(bg, p)];
@@ -425,48 +478,25 @@ __global__ void __launch_bounds__(THREADS, RESIDENT) dense_kernel(const __grid_c
                     finish_store(v, lane, S, bl, r, p, sv);
                 }
             } else if (p.S > 1) {            // partial of a clustered block: stays in red, added after the loop
-            } else if (!from_zero) {         // a later k-slice: publish the partial, tagged, in this CTA's slot
-                uint64_t* zs = p.Z + (size_t)c * p.M * 128;
-                for (int r = warp; r < p.M; r += CWARPS) {
-                    const float4 q = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-                    uint64_t* w = zs + r * 128 + 4 * lane;
-                    st_relaxed_v2_u64(w, TAG | __float_as_uint(q.x), TAG | __float_as_uint(q.y));
-                    st_relaxed_v2_u64(w + 2, TAG | __float_as_uint(q.z), TAG | __float_as_uint(q.w));
-                }
-            } else {                         // the finisher: add the later k-slices' partials in k order
-                const int c_hi = cta_of(bg * p.KT + p.KT - 1, p);
-                const uint2 sv = load_svh(S, bl, lane);
-                for (int r = warp; r < p.M; r += CWARPS) {
-                    const float4 own = *reinterpret_cast<const float4*>(red + r * RED_STRIDE + 4 * lane);
-                    float v[4] = {0.f + own.x, 0.f + own.y, 0.f + own.z, 0.f + own.w};
-                    for (int c4 = c + 1; c4 <= c_hi; c4 += 4) {   // 4 slots' reads in flight, then added in order
-                        float4 f[4];
-                        uint32_t ok = 0;
-    #pragma unroll
-                        for (int d = 0; d < 4; ++d)
-                            if (c4 + d <= c_hi) {
-                                const uint64_t* w = p.Z + ((size_t)(c4 + d) * p.M + r) * 128 + 4 * lane;
-                                uint64_t a, b, cc, dd;
-                                ld_relaxed_v2_u64(w, a, b);
-                                ld_relaxed_v2_u64(w + 2, cc, dd);
-                                f[d] = make_float4(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b),
-                                                   __uint_as_float((uint32_t)cc), __uint_as_float((uint32_t)dd));
-                                ok |= (((a & b & cc & dd) >> 32) != 0 ? 1u : 0u) << d;
-                            }
-    #pragma unroll
-                        for (int d = 0; d < 4; ++d)
-                            if (c4 + d <= c_hi) {
-                                uint64_t* w = p.Z + ((size_t)(c4 + d) * p.M + r) * 128 + 4 * lane;
-                                if (!((ok >> d) & 1u)) f[d] = poll_tagged4(w);
-                                v[0] += f[d].x; v[1] += f[d].y; v[2] += f[d].z; v[3] += f[d].w;
-                                st_relaxed_v2_u64(w, 0ull, 0ull);       // the slot is empty again
-                                st_relaxed_v2_u64(w + 2, 0ull, 0ull);
-                            }
-                    }
-                    finish_store(v, lane, S, bl, r, p, sv);
+            } else {
+                // equal k-slices: slice j stores the rows it does not finish and finishes the rows r = j (mod S), so
+                // the S CTAs of a block share the finishing; otherwise a later k-slice stores its whole partial and the
+                // CTA holding the block's first k-tile (its last segment) finishes every row
+                const int nsl = p.kslices, j = nsl > 1 ? c % nsl : 0;
+                const bool fin = nsl > 1 || from_zero;
+                if (nsl > 1 || !from_zero) store_partial(p, red, c, warp, lane, [&](int r) { return nsl > 1 && r % nsl == j; });
+                if (fin) {
+                    const int c0 = c - j, n = nsl > 1 ? nsl : cta_of(bg * p.KT + p.KT - 1, p) - c + 1;
+                    const int step = nsl > 1 ? nsl : 1;
+                    const uint2 sv = load_svh(S, bl, lane);
+                    for (int r = j + step * warp; r < p.M; r += step * CWARPS) finish_row(p, red, c0, n, j, r, S, bl, sv, lane);
                 }
             }
             named_sync(1, CT);   // red (and the rotation buffer) are reused by the next segment
+    #pragma unroll
+            for (int e = 0; e < 2; ++e)   // zeroed here, not above: dead, not zero, while the block is finished
+    #pragma unroll
+                for (int q = 0; q < NTG; ++q) acc[e][q][0] = acc[e][q][1] = acc[e][q][2] = acc[e][q][3] = 0.f;
             if (kt == p.KT) {
                 kt = 0;
                 ++bg;
@@ -666,13 +696,15 @@ bool ahead_enabled() {
     return on;
 }
 
-// With fewer blocks than SMs, ESPALIER_DENSE_SPLIT=slices gives every block S = SMs / blocks equal k-slices (one
-// segment a CTA, G = blocks * S CTAs); the default, ranges, splits the units in one equal range an SM (every SM busy,
-// a CTA meeting at most two blocks), used when every CTA's units fit the shared memory decoded.
+// With fewer blocks than SMs the default gives every block S = SMs / blocks equal k-slices (one segment a CTA,
+// G = blocks * S CTAs). ESPALIER_DENSE_SPLIT=ranges splits the units in one equal range an SM instead (every SM busy,
+// a CTA meeting at most two blocks), when every CTA's units fit the shared memory decoded: measured slower (0.87 vs
+// 0.80 ms for 40 config-2 blocks at batch 1, 1.76 vs 1.55 ms at 32 rows), a CTA's second segment adding its own
+// rotation, reduction and partial after the launch wait.
 bool split_ranges() {
     static const bool on = [] {
         const char* v = std::getenv("ESPALIER_DENSE_SPLIT");
-        return !(v && std::strcmp(v, "slices") == 0);
+        return v && std::strcmp(v, "ranges") == 0;
     }();
     return on;
 }
@@ -816,11 +848,10 @@ int dense_plan(const void* x, int x_dtype, long long x_stride, int m, int k, con
             if (dense_smem_bytes(K, 1, true, chunks_for(G), nmax, st) <= SMEM_LIMIT) return st;
         return 0;
     };
-    // Fewer blocks than SMs: one equal range of units an SM when every CTA's units fit the shared memory decoded
-    // (split_ranges; every SM busy, a CTA meeting at most two blocks), else S CTAs a block, each an equal k-slice (one
-    // segment a CTA, a block's S partials). Otherwise one range an SM over whole blocks, with at most a partial block
-    // at each end. The choice depends on the shape alone (not on the rows), so a row's bits do not depend on the
-    // others.
+    // Fewer blocks than SMs: S CTAs a block, each an equal k-slice (one segment a CTA, a block's S partials), or with
+    // split_ranges one equal range of units an SM when every CTA's units fit the shared memory decoded. Otherwise one
+    // range an SM over whole blocks, with at most a partial block at each end. The choice depends on the shape alone
+    // (not on the rows), so a row's bits do not depend on the others.
     const bool few = nbt < sms;
     p.G = few ? nbt * std::min(sms / nbt, p.KT) : sms;
     if (few && split_ranges() && !cluster_enabled() && ahead_stages(std::min(sms, p.U))) p.G = std::min(sms, p.U);
@@ -828,6 +859,9 @@ int dense_plan(const void* x, int x_dtype, long long x_stride, int m, int k, con
     // k-slices of a block finish inside one thread-block cluster when there are 2..16 of them (the limit of a
     // non-portable cluster on this GPU)
     p.S = (few && p.G % nbt == 0 && cluster_enabled() && p.G / nbt >= 2 && p.G / nbt <= 16) ? p.G / nbt : 0;
+    // above 8 rows a block's finishing is shared by its k-slices (measured: 1.20 vs 1.55 ms a 40-block step at 32
+    // rows); up to 8 rows the first slice finishes alone (0.80 vs 0.81 ms at 1 row, 0.90 vs 1.01 ms at 8 rows)
+    p.kslices = (few && p.G % nbt == 0 && p.G / nbt >= 2 && m > 8) ? p.G / nbt : 0;
     p.scale = cb_step(cb);
     p.Z = reinterpret_cast<uint64_t*>(z);
     const size_t zneed = (size_t)p.G * m * 128 * 8;

@@ -212,9 +212,10 @@ class EPLayer:
 
     def _expert_kernels(self, rows: int, lpf: torch.Tensor):
         """The y rows of every slot with a local pick (xg / xu rotated, the grouping in ids / count / members); no
-        combine here (n_routed 0: the home rank combines)."""
+        combine here (n_routed 0: the home rank combines). The one-launch kernel holds up to 32 rows; above (world x R
+        received rows) the two launches run."""
         e, L, slots = ext(), self.L, self.slots
-        if X.MOE_ONE_LAUNCH:
+        if X.MOE_ONE_LAUNCH and rows <= 32:
             e.moe_layer(self.xg, self.xu, L, self.ids, self.count, self.members, lpf, self.no_w, slots, 0, rows, self.S,
                         self.z, self.xd, self.y, self.cnt_layer, self.no_out[:rows], None)
         else:
