@@ -282,7 +282,7 @@ int esp_wait_flag(const int* flag, int need, int* result, void* stream);
  * esp_ipc_close / esp_ipc_free undo them. Inboxes of a rank: x rows [world][R][D] (x's dtype), picks int32
  * [world][R][slots], y fp32 [R][slots][D], flags_x and flags_y int32 [world]; plus a local epoch word and counters,
  * zero at allocation. Every rank calls with the same R, slots and world; a layer is the routing (esp_route_group of
- * this rank's rows, global ids), then:
+ * this rank's rows, global ids), then esp_ep_in, the experts, esp_ep_out:
  *
  *   esp_ep_in   x [R][D] (row stride x_stride) and pick [R][slots] (global ids, the shared slot last) of this rank's
  *               rows: each row to the ranks that own one of its routed picks (and to its own rank, which computes its
@@ -291,10 +291,13 @@ int esp_wait_flag(const int* flag, int need, int* result, void* stream);
  *               int32 [world][R][slots] (local expert ids, the local shared entry nl for this rank's own shared
  *               slots, -1 elsewhere), its grouping (uids / ucount / members as esp_group with maxm <= 32), and the
  *               received rows' rotation for the experts (xg / xu [world R slots][D] fp16, as esp_rot_in with the
- *               stacked suh of the local table's nl + 1 entries); counter: 2 int32 words, zero, left zero
- *   the expert layer (esp_moe_layer with n_routed = 0 over world * R rows: y fp32 [world][R][slots][D])
- *   esp_ep_out  each locally computed slot's y row to its home rank's inbox (inbox_y / flags_y: host arrays of
- *               every rank's bases; done: int32 [world], zero, left zero), then, once every owner's flag is seen,
+ *               stacked suh of the local table's nl + 1 entries)
+ *   esp_moe_layer_ep  the expert layer over rows = world * R <= 32 received rows (esp_moe_layer's arguments, no
+ *               combine): each slot's y row is stored straight into its home rank's inbox_y, and the launch's last
+ *               CTA releases every home's flags_y word for this rank; scratch_out: [rows][D] fp32, not read
+ *   esp_ep_out  unless `returned` (the rows came from esp_moe_layer_ep), first each locally computed slot's y row
+ *               (y fp32 [world][R][slots][D] of esp_moe_layer / esp_moe_down with n_routed = 0) to its home rank's
+ *               inbox and the flag (done: int32 [world], zero, left zero); then, once every owner's flag is seen,
  *               out / out_shared [R][D] as esp_ep_combine (slot-ordered fp32 fused multiply-adds; bit-identical to
  *               one GPU); advances *epoch; count: an int32 counter, zero, left zero
  *
@@ -309,10 +312,18 @@ int esp_ipc_free(void* ptr);
 int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots, int n_routed,
               int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick, int* const* flags_x,
               const int* epoch, int* local_pick, int* uids, int* ucount, int* members, int maxm, int maxu,
-              const void* suh_gate, const void* suh_up, void* xg, void* xu, int* counter, void* stream);
+              const void* suh_gate, const void* suh_up, void* xg, void* xu, void* stream);
+int esp_moe_layer_ep(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u,
+                     const int64_t* tp_d, const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g,
+                     const int* cb_u, const int* cb_d, const int* k2_host, const int* cb_host, int E,
+                     const uint16_t* svh_g, const uint16_t* svh_u, const uint16_t* suh_d, const uint16_t* svh_d,
+                     const int* uids, const int* ucount, const int* members, int maxu, int maxm,
+                     const int* local_pick, const float* no_w, int slots, int rows, int D, int I, int S, float* Z,
+                     uint16_t* xd, int* counters, float* const* inbox_y, int* const* flags_y, const int* epoch,
+                     int world, int rank, int R, float* scratch_out, void* stream);
 int esp_ep_out(const float* y, const int* local_pick, int world, int rank, int R, int slots, int n_routed, int E,
                int D, float* const* inbox_y, int* const* flags_y, const int* pick, const float* wts, void* out,
-               void* out_shared, int out_dtype, int* epoch, int* done, int* count, void* stream);
+               void* out_shared, int out_dtype, int* epoch, int* done, int* count, int returned, void* stream);
 
 #ifdef __cplusplus
 }

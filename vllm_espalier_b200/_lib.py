@@ -68,8 +68,10 @@ SIGNATURES = {
     "esp_ipc_close": (I, [P]),
     "esp_ipc_free": (I, [P]),
     "esp_ep_in": (I, [P, I, L, I, I, P, I, I, I, I, I, C.POINTER(P), C.POINTER(P), C.POINTER(P), P, P, P, P, P, I, I,
-                      P, P, P, P, P, P]),
-    "esp_ep_out": (I, [P, P, I, I, I, I, I, I, I, C.POINTER(P), C.POINTER(P), P, P, P, P, I, P, P, P, P]),
+                      P, P, P, P, P]),
+    "esp_moe_layer_ep": (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, P, P, P, I, I, P, P, I, I, I, I, I,
+                             P, P, P, C.POINTER(P), C.POINTER(P), P, I, I, I, P, P]),
+    "esp_ep_out": (I, [P, P, I, I, I, I, I, I, I, C.POINTER(P), C.POINTER(P), P, P, P, P, I, P, P, P, I, P]),
 }
 
 
@@ -317,6 +319,22 @@ class _Ext:
                                   pick.data_ptr(), wts.data_ptr(), slots, int(n_routed), rows, L.D, L.I, int(S),
                                   z.data_ptr(), xd.data_ptr(), y.data_ptr(), counters.data_ptr(), out.data_ptr(),
                                   ptr(out_shared), DTYPE[out.dtype], stream_ptr(xg.device)))
+
+    @staticmethod
+    def moe_layer_ep(xg, xu, L, uids, ucount, members, local_pick, no_w, slots, rows, S, z, xd, counters, inbox_y,
+                     flags_y, epoch, world, rank, R, scratch_out):
+        """esp_moe_layer for the expert-parallel layer: y rows into their home ranks' inboxes (inbox_y / flags_y:
+        ctypes arrays of every rank's addresses), flags released by the launch."""
+        k2h, cbh = L.host_tables("all")
+        g, u, d = L.gate, L.up, L.down
+        check(lib().esp_moe_layer_ep(xg.data_ptr(), xu.data_ptr(), g.ptr.data_ptr(), u.ptr.data_ptr(), d.ptr.data_ptr(),
+                                     g.k2.data_ptr(), u.k2.data_ptr(), d.k2.data_ptr(), g.cb.data_ptr(),
+                                     u.cb.data_ptr(), d.cb.data_ptr(), k2h.data_ptr(), cbh.data_ptr(), L.E,
+                                     g.svh.data_ptr(), u.svh.data_ptr(), d.suh.data_ptr(), d.svh.data_ptr(),
+                                     uids.data_ptr(), ucount.data_ptr(), members.data_ptr(), uids.numel(),
+                                     members.size(1), local_pick.data_ptr(), no_w.data_ptr(), slots, rows, L.D, L.I,
+                                     int(S), z.data_ptr(), xd.data_ptr(), counters.data_ptr(), inbox_y, flags_y,
+                                     epoch, world, rank, R, scratch_out.data_ptr(), stream_ptr(xg.device)))
 
     @staticmethod
     def moe_down(xd, L, uids, ucount, members, pick, wts, slots, n_routed, rows, y, counters, out, out_shared):

@@ -94,7 +94,6 @@ struct InParams {
     int* uids; int* ucount; int* members;
     int maxm, maxu;
     RotIn rot;                         // suh (stacked [nl + 1][D], gate / up) and the rotated rows [world R slots][D]
-    int* counter;                      // 2 words, zero on entry and left zero
 };
 
 // Dispatch, receive, group and rotate in one launch (see the top of the file). x of dtype T.
@@ -123,50 +122,38 @@ __global__ void __launch_bounds__(EP_THREADS) ep_in_kernel(const __grid_constant
             for (int c = lane; c < D / 8; c += 32) dst[c] = src[c];
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            st_release_sys(p.flags_x.ptr[q] + p.rank, *p.epoch + 1);
-        }
+        // the release is cumulative over the CTA's stores ordered before it by the barrier: no separate fence
+        if (threadIdx.x == 0) st_release_sys(p.flags_x.ptr[q] + p.rank, *p.epoch + 1);
     }
     const int e0 = p.rank * p.E / p.world, e1 = (p.rank + 1) * p.E / p.world, nl = e1 - e0;
     const int n = p.world * R * slots;
-    if (blockIdx.x == 0) {             // ---- receive: every source's flag, the local table and its grouping ----
-        if (threadIdx.x == 0) {
-            const int need = *p.epoch + 1;
-            bool ok = true;
-            for (int s = 0; s < p.world && ok; ++s) ok = wait_flag_sys(p.my_flags + s, need);
-            s_ok = ok;
-        }
-        __syncthreads();
+    // ---- receive: every CTA waits for every source's flag itself (no publication step inside the launch) ----
+    if (threadIdx.x == 0) {
+        const int need = *p.epoch + 1;
+        bool ok = true;
+        for (int s = 0; s < p.world && ok; ++s) ok = wait_flag_sys(p.my_flags + s, need);
+        s_ok = ok;
+    }
+    __syncthreads();
+    // slot i's local entry: a routed pick owned here -> its local id, this rank's own shared slot -> nl, else -1
+    auto local_of = [&](int i) -> int {
+        if (!s_ok) return -1;
+        const int e = __ldcv(p.my_pick + i);
+        const int j = i % slots, src = i / (R * slots);
+        if (j < p.n_routed) return (e >= e0 && e < e1) ? e - e0 : -1;
+        return (src == p.rank && e >= 0) ? nl : -1;
+    };
+    if (blockIdx.x == 0) {             // the local table and its grouping, for the expert kernel
         for (int i = threadIdx.x; i < n; i += EP_THREADS) {
-            int v = -1;
-            if (s_ok) {
-                const int e = __ldcv(p.my_pick + i);
-                const int j = i % slots, src = i / (R * slots);
-                if (j < p.n_routed) v = (e >= e0 && e < e1) ? e - e0 : -1;
-                else v = (src == p.rank && e >= 0) ? nl : -1;   // the shared slot: computed on the row's home rank
-            }
+            const int v = local_of(i);
             sh_lp[i] = v;
             p.lp[i] = v;
         }
         __syncthreads();
         group_block(sh_lp, n, slots, nl + 1, p.uids, p.ucount, p.members, p.maxm, p.maxu);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            st_release_gpu(p.counter, 1);
-        }
     }
-    // ---- rotate: every CTA, once the table is published ----
-    __shared__ int s_go;
-    if (threadIdx.x == 0) s_go = wait_flag_gpu(p.counter, 1);
-    __syncthreads();
-    if (s_go) rotate_share<T>(reinterpret_cast<const T*>(p.inbox_x.ptr[p.rank]), D, D, p.lp, n, slots, p.rot);
-    __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(p.counter + 1, 1) == (int)gridDim.x - 1) {   // every CTA is past its wait
-        p.counter[0] = 0;
-        p.counter[1] = 0;
-    }
+    // ---- rotate a share of the received slots (rot_in's arithmetic), each slot's entry from the picks directly ----
+    rotate_share_by<T>(reinterpret_cast<const T*>(p.inbox_x.ptr[p.rank]), D, D, n, slots, p.rot, local_of);
 }
 
 struct OutParams {
@@ -196,7 +183,7 @@ __global__ void __launch_bounds__(EP_THREADS) ep_out_kernel(const __grid_constan
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = p.R, D = p.D, slots = p.slots;
     const int need = *p.epoch + 1;
-    const int nret = p.world * p.split;
+    const int nret = p.world * p.split;   // 0: the expert kernel stored the y rows and released the flags itself
     if ((int)blockIdx.x < nret) {      // ---- return: this rank's y rows of home h's slots ----
         const int h = blockIdx.x / p.split, part = blockIdx.x % p.split;
         const int wpc = EP_THREADS / 32, nw = wpc * p.split;
@@ -209,13 +196,11 @@ __global__ void __launch_bounds__(EP_THREADS) ep_out_kernel(const __grid_constan
             for (int c = lane; c < D / 4; c += 32) d[c] = __ldcg(src + c);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();   // this CTA's stores before the arrival that may release the flag
-            if (atomicAdd(p.done + h, 1) == p.split - 1) {
-                __threadfence_system();
-                p.done[h] = 0;
-                st_release_sys(p.flags_y.ptr[h] + p.rank, need);
-            }
+        // the arrival releases this CTA's stores (cumulative over the barrier), the last one acquires the others'
+        // and its system-scope release of the flag publishes them all: no separate fences
+        if (threadIdx.x == 0 && arrive_acq_rel(p.done + h) == p.split - 1) {
+            p.done[h] = 0;
+            st_release_sys(p.flags_y.ptr[h] + p.rank, need);
         }
     } else {                           // ---- finish row r ----
         const int r = blockIdx.x - nret;
@@ -301,9 +286,9 @@ int esp_ipc_free(void* ptr) {
 int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, const int* pick, int slots, int n_routed,
               int E, int world, int rank, void* const* inbox_x, void* const* inbox_pick, int* const* flags_x,
               const int* epoch, int* local_pick, int* uids, int* ucount, int* members, int maxm, int maxu,
-              const void* suh_gate, const void* suh_up, void* xg, void* xu, int* counter, void* stream) {
+              const void* suh_gate, const void* suh_up, void* xg, void* xu, void* stream) {
     ESP_REQUIRE(x && pick && inbox_x && inbox_pick && flags_x && epoch && local_pick && uids && ucount && members &&
-                    suh_gate && suh_up && xg && xu && counter,
+                    suh_gate && suh_up && xg && xu,
                 ESP_ERR_INVALID, "ep_in: null pointer");
     ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world, ESP_ERR_INVALID,
                 "ep_in: 1 to %d ranks", EP_MAX_WORLD);
@@ -335,7 +320,6 @@ int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, cons
     p.rot.out[0] = static_cast<__half*>(xg);
     p.rot.out[1] = static_cast<__half*>(xu);
     p.rot.E_tab = nl + 1;
-    p.counter = counter;
     // about four rotation tasks (a matrix, a slot, a 128-block) a warp, at least a CTA a destination, one wave
     const int tasks = 2 * world * R * slots * (D / 128);
     const int grid = std::max(world, std::min(device_sms(), (tasks + 4 * (EP_THREADS / 32) - 1) / (4 * (EP_THREADS / 32))));
@@ -348,9 +332,9 @@ int esp_ep_in(const void* x, int x_dtype, long long x_stride, int R, int D, cons
 
 int esp_ep_out(const float* y, const int* local_pick, int world, int rank, int R, int slots, int n_routed, int E,
                int D, float* const* inbox_y, int* const* flags_y, const int* pick, const float* wts, void* out,
-               void* out_shared, int out_dtype, int* epoch, int* done, int* count, void* stream) {
-    ESP_REQUIRE(y && local_pick && inbox_y && flags_y && pick && wts && out && epoch && done && count, ESP_ERR_INVALID,
-                "ep_out: null pointer");
+               void* out_shared, int out_dtype, int* epoch, int* done, int* count, int returned, void* stream) {
+    ESP_REQUIRE(inbox_y && flags_y && pick && wts && out && epoch && count && (returned || (y && local_pick && done)),
+                ESP_ERR_INVALID, "ep_out: null pointer");
     ESP_REQUIRE(world >= 1 && world <= EP_MAX_WORLD && rank >= 0 && rank < world && R >= 1 && R <= 32 &&
                     slots >= 1 && slots <= 32 && n_routed <= slots && E >= world && D % 4 == 0,
                 ESP_ERR_INVALID, "ep_out: limits");
@@ -359,7 +343,7 @@ int esp_ep_out(const float* y, const int* local_pick, int world, int rank, int R
     OutParams p{};
     p.y = y; p.lp = local_pick;
     p.R = R; p.D = D; p.slots = slots; p.n_routed = n_routed; p.E = E; p.world = world; p.rank = rank;
-    p.split = R * slots > 64 ? 4 : 1;
+    p.split = returned ? 0 : R * slots > 64 ? 4 : 1;
     for (int q = 0; q < world; ++q) {
         ESP_REQUIRE(inbox_y[q] && flags_y[q], ESP_ERR_INVALID, "ep_out: rank %d's buffers", q);
         p.inbox_y.ptr[q] = inbox_y[q];

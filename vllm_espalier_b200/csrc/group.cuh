@@ -108,15 +108,16 @@ __device__ bool wait_flag_gpu(const int* flag, int need) {
     return false;
 }
 
-template <typename T>
-__device__ void rotate_share(const T* __restrict__ x, long long x_stride, int H, const int* pick, int P, int slots,
-                             const RotIn& rot) {
+// The rotation of the items (matrix, slot p, 128-block) with a pick in [0, E_tab): pick_of(p) gives slot p's entry.
+template <typename T, typename PickOf>
+__device__ void rotate_share_by(const T* __restrict__ x, long long x_stride, int H, int P, int slots, const RotIn& rot,
+                                PickOf pick_of) {
     const int lane = threadIdx.x & 31;
     const int nblk = H / 128, ntask = 2 * P * nblk;
     const int wpc = blockDim.x >> 5, nw = gridDim.x * gridDim.y * wpc;
     for (int w = (blockIdx.y * gridDim.x + blockIdx.x) * wpc + (threadIdx.x >> 5); w < ntask; w += nw) {
         const int mat = w / (P * nblk), rem = w % (P * nblk), p = rem / nblk, blk = rem % nblk;
-        const int e = __ldcg(pick + p);
+        const int e = pick_of(p);
         if (e < 0 || e >= rot.E_tab) continue;
         const int k0 = blk * 128 + 4 * lane;
         const __half* su = rot.suh[mat] + (size_t)e * H + k0;
@@ -134,6 +135,11 @@ __device__ void rotate_share(const T* __restrict__ x, long long x_stride, int H,
     }
 }
 
+template <typename T>
+__device__ void rotate_share(const T* __restrict__ x, long long x_stride, int H, const int* pick, int P, int slots,
+                             const RotIn& rot) {
+    rotate_share_by<T>(x, x_stride, H, P, slots, rot, [pick](int p) { return __ldcg(pick + p); });
+}
 
 }  // namespace
 }  // namespace esp

@@ -709,6 +709,13 @@ struct LayerParams {
     int* work;
     int* ready;
     int* exits;
+    // expert parallel (ep_world > 0): the y row of slot q = (home rank h, row r, slot j) of the received rows goes
+    // straight into h's inbox [R][slots][D] (a peer store), and the last CTA out releases every home's flag for this
+    // rank (epoch + 1); the rows' combine then runs on their home ranks
+    float* ep_y[8];
+    int* ep_flag[8];
+    const int* ep_epoch;
+    int ep_world, ep_rank, ep_R;
 };
 
 struct FinEntry {
@@ -1217,7 +1224,13 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
                     o.y = v[1] * HAD_SCALE * scale_at(sc.d, 1);
                     o.z = v[2] * HAD_SCALE * scale_at(sc.d, 2);
                     o.w = v[3] * HAD_SCALE * scale_at(sc.d, 3);
-                    *reinterpret_cast<float4*>(p.y + (size_t)d->rows[m] * p.D + n0) = o;
+                    const int q = d->rows[m];
+                    float* yr = p.y + (size_t)q * p.D;
+                    if (p.ep_world) {   // into the home rank's inbox: slot q of home h is its slot q - h R slots
+                        const int per = p.ep_R * p.slots, h = q / per;
+                        yr = p.ep_y[h] + (size_t)(q - h * per) * p.D;
+                    }
+                    *reinterpret_cast<float4*>(yr + n0) = o;
                 }
                 named_sync(1, CT);
                 if (warp == 0) enqueue(1, u, d);
@@ -1231,6 +1244,13 @@ __global__ void __launch_bounds__(LTHREADS, 1) layer_kernel(const __grid_constan
     if (threadIdx.x == 0 && arrive_acq_rel(p.exits) == (int)gridDim.x - 1) {
         for (int i = 0; i < p.maxu; ++i) p.ready[i] = 0;
         *p.exits = 0;
+        // every CTA's y stores are ordered before its arrival (release after the CTA barrier above), which this
+        // acquire saw: the system-scope release of each home's flag publishes them all
+        if (p.ep_world) {
+            const int v = *p.ep_epoch + 1;
+            for (int h = 0; h < p.ep_world; ++h)
+                asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p.ep_flag[h] + p.ep_rank), "r"(v) : "memory");
+        }
     }
 }
 
@@ -1587,13 +1607,13 @@ int esp_moe_down(const uint16_t* xd, const int64_t* tp_d, const int* k2_d, const
 
 // The fused expert layer in one launch: gate/up + SwiGLU and down + combine (the sequence of esp_moe_gateup and
 // esp_moe_down, the same output bits).
-int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u, const int64_t* tp_d,
+static int moe_layer_impl(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u, const int64_t* tp_d,
                   const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g, const int* cb_u, const int* cb_d,
                   const int* k2_host, const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u,
                   const uint16_t* suh_d, const uint16_t* svh_d, const int* uids, const int* ucount, const int* members,
                   int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed, int rows, int D, int I,
                   int S, float* Z, uint16_t* xd, float* y, int* counters, void* out, void* out_shared, int out_dtype,
-                  void* stream) {
+                  void* stream, const LayerParams* ep) {
     ESP_REQUIRE(xg && xu && tp_g && tp_u && tp_d && k2_g && k2_u && k2_d && cb_g && cb_u && cb_d && k2_host &&
                     cb_host && svh_g && svh_u && suh_d && svh_d && uids && ucount && members && pick && wts && xd &&
                     y && counters && out,
@@ -1631,8 +1651,59 @@ int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, c
     p.work = p.cnt_d + (size_t)rows * (D / 128);
     p.ready = p.work + 1;
     p.exits = p.ready + maxu;
+    if (ep) {
+        for (int h = 0; h < 8; ++h) {
+            p.ep_y[h] = ep->ep_y[h];
+            p.ep_flag[h] = ep->ep_flag[h];
+        }
+        p.ep_epoch = ep->ep_epoch;
+        p.ep_world = ep->ep_world;
+        p.ep_rank = ep->ep_rank;
+        p.ep_R = ep->ep_R;
+    }
     if (int rc = launch_layer(p, (maxm + 7) / 8, kmax, stream)) return rc;
     return ok();
+}
+
+int esp_moe_layer(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u, const int64_t* tp_d,
+                  const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g, const int* cb_u, const int* cb_d,
+                  const int* k2_host, const int* cb_host, int E, const uint16_t* svh_g, const uint16_t* svh_u,
+                  const uint16_t* suh_d, const uint16_t* svh_d, const int* uids, const int* ucount, const int* members,
+                  int maxu, int maxm, const int* pick, const float* wts, int slots, int n_routed, int rows, int D, int I,
+                  int S, float* Z, uint16_t* xd, float* y, int* counters, void* out, void* out_shared, int out_dtype,
+                  void* stream) {
+    return moe_layer_impl(xg, xu, tp_g, tp_u, tp_d, k2_g, k2_u, k2_d, cb_g, cb_u, cb_d, k2_host, cb_host, E, svh_g, svh_u,
+                          suh_d, svh_d, uids, ucount, members, maxu, maxm, pick, wts, slots, n_routed, rows, D, I, S, Z,
+                          xd, y, counters, out, out_shared, out_dtype, stream, nullptr);
+}
+
+int esp_moe_layer_ep(const uint16_t* xg, const uint16_t* xu, const int64_t* tp_g, const int64_t* tp_u,
+                     const int64_t* tp_d, const int* k2_g, const int* k2_u, const int* k2_d, const int* cb_g,
+                     const int* cb_u, const int* cb_d, const int* k2_host, const int* cb_host, int E,
+                     const uint16_t* svh_g, const uint16_t* svh_u, const uint16_t* suh_d, const uint16_t* svh_d,
+                     const int* uids, const int* ucount, const int* members, int maxu, int maxm,
+                     const int* local_pick, const float* no_w, int slots, int rows, int D, int I, int S, float* Z,
+                     uint16_t* xd, int* counters, float* const* inbox_y, int* const* flags_y, const int* epoch,
+                     int world, int rank, int R, float* scratch_out, void* stream) {
+    ESP_REQUIRE(inbox_y && flags_y && epoch && scratch_out && local_pick && no_w, ESP_ERR_INVALID,
+                "moe_layer_ep: null pointer");
+    ESP_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world && R >= 1 && rows == world * R, ESP_ERR_INVALID,
+                "moe_layer_ep: rows = world * R, 1 to 8 ranks");
+    LayerParams ep = {};
+    for (int h = 0; h < world; ++h) {
+        ESP_REQUIRE(inbox_y[h] && flags_y[h], ESP_ERR_INVALID, "moe_layer_ep: rank %d's inbox", h);
+        ep.ep_y[h] = inbox_y[h];
+        ep.ep_flag[h] = flags_y[h];
+    }
+    ep.ep_epoch = epoch;
+    ep.ep_world = world;
+    ep.ep_rank = rank;
+    ep.ep_R = R;
+    // no combine on this rank (n_routed 0): the finisher still counts each row's slots (the local picks) and leaves
+    // its counters zero; its row outputs go to scratch_out ([rows][D] fp32, unread)
+    return moe_layer_impl(xg, xu, tp_g, tp_u, tp_d, k2_g, k2_u, k2_d, cb_g, cb_u, cb_d, k2_host, cb_host, E, svh_g, svh_u,
+                          suh_d, svh_d, uids, ucount, members, maxu, maxm, local_pick, no_w, slots, 0, rows, D, I, S, Z,
+                          xd, scratch_out, counters, scratch_out, nullptr, ESP_DTYPE_F32, stream, &ep);
 }
 
 size_t esp_moe_layer_counters(int maxu, int rows, int D, int I) {

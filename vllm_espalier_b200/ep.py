@@ -181,7 +181,6 @@ class EPLayer:
         self.cnt_layer = torch.zeros((int(lib().esp_moe_layer_counters(self.maxu, world * rows, D, I)),),
                                      dtype=torch.int32, device=dev)
         self.no_w = torch.zeros((P,), dtype=torch.float32, device=dev)
-        self.in_counter = torch.zeros((2,), dtype=torch.int32, device=dev)   # esp_ep_in's publication words
         self.no_out = torch.empty((world * rows, D), dtype=torch.bfloat16, device=dev)
         self.exchange = EP_EXCHANGE
         self.ex = None          # the PeerExchange, made at the first p2p forward (it needs the rows' dtype)
@@ -245,7 +244,8 @@ class EPLayer:
 
     def _forward_p2p(self, x, gate, out, out_shared, group):
         """The same layer with the peer-store exchange, four launches: routing; esp_ep_in (dispatch, receive, grouping,
-        the experts' input rotation); the expert layer kernel; esp_ep_out (return, finish)."""
+        the experts' input rotation); the expert layer kernel, storing each slot's y row in its home rank's inbox (up to
+        32 received rows; above, the two expert launches and esp_ep_out's return step); esp_ep_out (the combine)."""
         R, D = x.shape
         if R > self.rows:
             raise ValueError(f"{R} rows a rank, the layer holds {self.rows}")
@@ -259,12 +259,18 @@ class EPLayer:
         check(h.esp_ep_in(x.data_ptr(), DTYPE[x.dtype], x.stride(0), R, D, pick.data_ptr(), slots, k, self.E, world,
                           rank, ex.peer["x"], ex.peer["pick"], ex.peer["flags_x"], ex.local("epoch"), lp.data_ptr(),
                           self.ids.data_ptr(), self.count.data_ptr(), self.members.data_ptr(), MAXM, self.maxu,
-                          L.gate.suh.data_ptr(), L.up.suh.data_ptr(), self.xg.data_ptr(), self.xu.data_ptr(),
-                          self.in_counter.data_ptr(), st))
-        self._expert_kernels(world * R, lp)
+                          L.gate.suh.data_ptr(), L.up.suh.data_ptr(), self.xg.data_ptr(), self.xu.data_ptr(), st))
+        rows = world * R
+        returned = X.MOE_ONE_LAUNCH and rows <= 32
+        if returned:    # the expert kernel stores each slot's y row in its home rank's inbox and releases the flags
+            ext().moe_layer_ep(self.xg, self.xu, L, self.ids, self.count, self.members, lp, self.no_w, slots, rows,
+                               self.S, self.z, self.xd, self.cnt_layer, ex.peer["y"], ex.peer["flags_y"],
+                               ex.local("epoch"), world, rank, R, self.y)
+        else:
+            self._expert_kernels(rows, lp)
         out = out if out is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
         out_shared = out_shared if out_shared is not None else torch.empty((R, D), dtype=x.dtype, device=x.device)
         check(h.esp_ep_out(self.y.data_ptr(), lp.data_ptr(), world, rank, R, slots, k, self.E, D, ex.peer["y"],
                            ex.peer["flags_y"], pick.data_ptr(), wts.data_ptr(), out.data_ptr(), out_shared.data_ptr(),
-                           DTYPE[out.dtype], ex.local("epoch"), ex.local("done"), ex.local("count"), st))
+                           DTYPE[out.dtype], ex.local("epoch"), ex.local("done"), ex.local("count"), int(returned), st))
         return out, out_shared
