@@ -403,17 +403,18 @@ def route_bench(dev, steps: int, warmup: int, dist, call, picks) -> dict:
 
 
 def our_route(dev):
+    """The fused routing kernel on its own (ext().route_group: GEMV, top-k, renormalisation, shared gate, grouping)."""
     from vllm_espalier_b200 import experts as G
-
-    class _L:   # what route() reads of a layer
-        pass
+    from vllm_espalier_b200._lib import ext
     gate, sgate, _ = route_inputs(dev)
-    L = _L()
-    L.gate_w, L.shared_id = sgate, MOE_E
     s = G.Scratch(MOE_E + 1, MOE_D, MOE_I, 32, MOE_K + 1, dev)
 
     def call(x, g):
-        G.route(x, g, MOE_K, L, s)
+        R = x.shape[0]
+        ids, members = s.window(R)
+        n = R * s.slots
+        ext().route_group(x, g, sgate, MOE_K, MOE_E, s.logits, s.route_counter, s.pick[:n], s.wts[:n], ids, s.count,
+                          members)
 
     def picks(R):
         return s.pick[:R * (MOE_K + 1)].view(R, MOE_K + 1)[:, :MOE_K].cpu().numpy()
