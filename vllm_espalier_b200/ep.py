@@ -19,8 +19,8 @@ layer, with outputs bit-identical to it for every world size:
 The exchange (ESPALIER_EP_EXCHANGE): `p2p` (default) moves rows and results by stores into the other ranks' memory
 (csrc/ep.cu, PeerExchange below): a row goes only to the ranks owning one of its picks, a slot's y row only from its
 owner to its home rank, with release / acquire flags instead of collectives; a layer is four launches (routing,
-esp_ep_in = dispatch + receive + grouping + rotation, the one-launch expert kernel, esp_ep_out = return + combine)
-and nothing on the host; `nccl` is the two-collective form above. The index logic of the `nccl` form (local
+esp_ep_in = dispatch + receive + grouping + rotation, the one-launch expert kernel storing each slot's y row in its
+home rank's inbox, esp_ep_out = the combine) and nothing on the host; `nccl` is the two-collective form above. The index logic of the `nccl` form (local
 tables, owners, buffer layouts) is in plain torch functions shared with the CPU tests (gloo ranks with a stand-in
 expert function); the `p2p` form computes the same table on the device (esp_ep_in).
 """
