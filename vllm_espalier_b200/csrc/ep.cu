@@ -8,12 +8,14 @@
 //   esp_ep_in   (dispatch) CTA q < world stores every row of this rank that has a routed pick owned by rank q (all
 //               rows when q is this rank, which computes their shared slots) and every row's pick list into rank q's
 //               inboxes, then a release store of the call's epoch into q's flag word for this source;
-//               (receive) CTA 0 waits (bounded) for every source's flag, writes the local pick table (a pick owned
-//               here becomes its local expert id, the shared slot of this rank's own rows the local shared entry,
-//               every other slot -1) and its grouping (esp_group's), and publishes them;
-//               (rotate) then every CTA rotates a share of the received slots' rows for the expert kernels (rot_in)
-//   esp_ep_out  (return) CTAs (h, part) store each locally computed slot's y row (D fp32) into its home rank h's
-//               inbox, then a release flag per home rank: only owned slots cross NVLink;
+//               (receive) every CTA waits (bounded) for every source's flag; CTA 0 writes the local pick table (a pick
+//               owned here becomes its local expert id, the shared slot of this rank's own rows the local shared
+//               entry, every other slot -1) and its grouping (esp_group's); every CTA rotates a share of the received
+//               slots' rows for the expert kernel (rot_in), mapping each slot's pick to its local entry itself
+//   the expert kernel (esp_moe_layer_ep, moe.cu) stores each slot's y row into its home rank's inbox and releases the
+//               flags; above 32 received rows the two-launch expert kernels write y locally and esp_ep_out returns it
+//   esp_ep_out  (return, only then) CTAs (h, part) store each locally computed slot's y row (D fp32) into home rank
+//               h's inbox, then a release flag per home rank: only owned slots cross NVLink;
 //               (finish) CTA r waits (bounded) for every owner's flag and combines row r's routed slots in slot order
 //               with fp32 fused multiply-adds from 0 and the gated shared slot (the single-GPU layer's arithmetic on
 //               the same y values, so outputs are bit-identical to one GPU); the last CTA advances the epoch
@@ -211,22 +213,46 @@ __global__ void __launch_bounds__(EP_THREADS) ep_out_kernel(const __grid_constan
         }
         __syncthreads();
         if (s_ok) {
+            // four columns a thread at a time, eight slots' loads in flight before their fused multiply-adds (the
+            // same per-element order as one slot after the other: slot order from 0, picks outside [0, E) skipped)
             T* out = static_cast<T*>(p.out);
             T* out_shared = static_cast<T*>(p.out_shared);
-            for (int c = threadIdx.x; c < D; c += EP_THREADS) {
-                float acc = 0.f;
-                for (int j = 0; j < p.n_routed; ++j) {
-                    const int e = p.pick[r * slots + j];
-                    if (e < 0 || e >= p.E) continue;
-                    acc = __fmaf_rn(p.wts[r * slots + j], __ldcv(p.my_y + ((size_t)r * slots + j) * D + c), acc);
+            const float* yr = p.my_y + (size_t)r * slots * D;
+            const int* pk = p.pick + r * slots;
+            const float* wt = p.wts + r * slots;
+            for (int c = 4 * threadIdx.x; c < D; c += 4 * EP_THREADS) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int j0 = 0; j0 < p.n_routed; j0 += 8) {
+                    float4 v[8];
+                    bool on[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int j = j0 + q;
+                        on[q] = j < p.n_routed && pk[j] >= 0 && pk[j] < p.E;
+                        if (on[q]) v[q] = __ldcv(reinterpret_cast<const float4*>(yr + (size_t)j * D + c));
+                    }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        if (on[q]) {
+                            const float w = wt[j0 + q];
+                            acc[0] = __fmaf_rn(w, v[q].x, acc[0]);
+                            acc[1] = __fmaf_rn(w, v[q].y, acc[1]);
+                            acc[2] = __fmaf_rn(w, v[q].z, acc[2]);
+                            acc[3] = __fmaf_rn(w, v[q].w, acc[3]);
+                        }
                 }
-                out[(size_t)r * D + c] = from_f32<T>(acc);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) out[(size_t)r * D + c + i] = from_f32<T>(acc[i]);
                 if (out_shared && slots > p.n_routed) {
                     const int j = p.n_routed;
-                    const float v = p.pick[r * slots + j] >= 0
-                                        ? p.wts[r * slots + j] * __ldcv(p.my_y + ((size_t)r * slots + j) * D + c)
-                                        : 0.f;
-                    out_shared[(size_t)r * D + c] = from_f32<T>(v);
+                    float sh[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (pk[j] >= 0) {
+                        const float4 y4 = __ldcv(reinterpret_cast<const float4*>(yr + (size_t)j * D + c));
+                        const float w = wt[j];
+                        sh[0] = w * y4.x; sh[1] = w * y4.y; sh[2] = w * y4.z; sh[3] = w * y4.w;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) out_shared[(size_t)r * D + c + i] = from_f32<T>(sh[i]);
                 }
             }
         }
