@@ -1390,16 +1390,28 @@ __global__ void __launch_bounds__(32) ep_combine_kernel(const float* __restrict_
     const int r = blockIdx.x, lane = threadIdx.x;
     const int n0 = blockIdx.y * 128 + 4 * lane;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < n_routed; ++j) {
-        const int e = pick[r * slots + j];
-        if (e < 0 || e >= E_routed) continue;
-        const int owner = ((e + 1) * world - 1) / E_routed;
-        const float w = wts[r * slots + j];
-        const float4 y = *reinterpret_cast<const float4*>(recv_y + (((size_t)owner * R + r) * slots + j) * D + n0);
-        acc[0] = fmaf(w, y.x, acc[0]);
-        acc[1] = fmaf(w, y.y, acc[1]);
-        acc[2] = fmaf(w, y.z, acc[2]);
-        acc[3] = fmaf(w, y.w, acc[3]);
+    for (int j0 = 0; j0 < n_routed; j0 += 8) {   // eight slots' loads in flight, then added in slot order
+        float4 y[8];
+        bool on[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int j = j0 + q;
+            const int e = j < n_routed ? pick[r * slots + j] : -1;
+            on[q] = e >= 0 && e < E_routed;
+            if (on[q]) {
+                const int owner = ((e + 1) * world - 1) / E_routed;
+                y[q] = *reinterpret_cast<const float4*>(recv_y + (((size_t)owner * R + r) * slots + j) * D + n0);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            if (on[q]) {
+                const float w = wts[r * slots + j0 + q];
+                acc[0] = fmaf(w, y[q].x, acc[0]);
+                acc[1] = fmaf(w, y[q].y, acc[1]);
+                acc[2] = fmaf(w, y[q].z, acc[2]);
+                acc[3] = fmaf(w, y[q].w, acc[3]);
+            }
     }
     store4(out, out_dtype, (size_t)r * D + n0, acc);
     if (out_shared && n_routed < slots) {
