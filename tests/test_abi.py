@@ -37,6 +37,26 @@ def test_signatures_cover_header():
     assert set(declared_symbols()) <= set(_lib.SIGNATURES), "every declared entry point has a ctypes signature"
 
 
+def declared_arity():
+    """name -> number of parameters of each declaration in include/*.h."""
+    out = {}
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(esp_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text):
+            params = m.group(2).strip()
+            out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_signatures_match_header_arity():
+    """Every ctypes signature has as many arguments as its C declaration: a mismatch would pass garbage through the
+    ABI instead of failing."""
+    arity = declared_arity()
+    assert arity, "no declarations parsed"
+    bad = {n: (k, len(_lib.SIGNATURES[n][1])) for n, k in arity.items() if len(_lib.SIGNATURES[n][1]) != k}
+    assert not bad, f"header vs ctypes argument counts: {bad}"
+
+
 def test_host_validation_without_gpu():
     lib = _lib.lib()
     assert lib.esp_version() >= 100
