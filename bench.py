@@ -62,7 +62,7 @@ def block_bytes() -> int:
 # synthetic coded matrices (torch only: both arms build the same weights from the same seeds)
 # ---------------------------------------------------------------------------------------------------------------
 class Mat:
-    """A random coded matrix: uniform int16 trellis, +-1 suh, +-U(0.5, 1.5)/64 svh (SURVEY's synthetic inputs)."""
+    """A random coded matrix: uniform int16 trellis, +-1 suh, +-U(0.5, 1.5)/64 svh (the synthetic stand-in for a checkpoint)."""
 
     def __init__(self, kin, n, K, grid, gen, dev):
         self.trellis = torch.randint(-32768, 32768, (kin // 16, n // 16, 16 * K), dtype=torch.int16, device=dev,
